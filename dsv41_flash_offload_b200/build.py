@@ -1,0 +1,70 @@
+"""Build the sm_100a C-ABI library libdsv41_b200.so in-tree with nvcc.
+
+    python -m dsv41_flash_offload_b200.build [--verbose]
+
+nvcc -gencode arch=compute_100a,code=sm_100a -lineinfo -O3; the CUDA runtime is linked
+statically so the library only needs the driver (and coexists with torch's own runtime).
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+LIB = os.path.join(HERE, "libdsv41_b200.so")
+SOURCES = ["capi.cu", "permute.cu", "transform.cu", "gemv.cu", "gemm.cu"]
+HEADERS = ["common.cuh", "internal.h", "gemm.h"]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc_path() -> str:
+    for p in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc"):
+        if p and os.path.exists(p):
+            return p
+    return "nvcc"
+
+
+def nvcc_version(nvcc: str) -> str:
+    out = subprocess.run([nvcc, "--version"], capture_output=True, text=True).stdout
+    for line in out.splitlines():
+        if "release" in line:
+            return line.split("release")[-1].strip().split(",")[0]
+    return "unknown"
+
+
+def needs_build() -> bool:
+    if not os.path.exists(LIB):
+        return True
+    t = os.path.getmtime(LIB)
+    deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS] + [os.path.join(HERE, "..", "include", "dsv41_b200.h")]
+    return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
+
+
+def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = False) -> str:
+    if not force and not needs_build():
+        return LIB
+    nvcc = nvcc_path()
+    ver = nvcc_version(nvcc)
+    cmd = [nvcc, *ARCH, "-lineinfo", "-O3", "-std=c++17", "--use_fast_math=false", "-shared",
+           "-Xcompiler", "-fPIC", "-cudart", "static", f'-DDSV41_NVCC_VERSION="{ver}"',
+           "-o", LIB + ".tmp"] + [os.path.join(CSRC, s) for s in SOURCES]
+    cmd = [c for c in cmd if c != "--use_fast_math=false"]
+    if ptxas_verbose:
+        cmd.insert(1, "-Xptxas=-v")
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError("nvcc failed building libdsv41_b200.so")
+    if verbose or ptxas_verbose:
+        sys.stderr.write(r.stderr)
+    os.replace(LIB + ".tmp", LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    build(verbose="--verbose" in sys.argv, force=True, ptxas_verbose="--ptxas" in sys.argv)
+    print(LIB)

@@ -1,0 +1,462 @@
+// C ABI of the B200 routed-expert MoE path (declared in include/dsv41_b200.h).
+//
+// dsv41_moe_forward replaces apply_exl3_fused_moe (patches/vllm-exl3-host-dma.patch:203-449,
+// wrapped in the reference by ct/ct_vllm.py:181-225): permute -> row transforms -> decode-GEMV
+// gate/up (+act, down-input transform) -> decode-GEMV down -> busy-expert GEMM -> combine,
+// all on the caller's stream, nothing allocated, no host synchronisation (CUDA-graph safe).
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/dsv41_b200.h"
+#include "common.cuh"
+#include "gemm.h"
+#include "internal.h"
+
+namespace dsv41 {
+
+static thread_local std::string g_last_error;
+
+static int fail(int code, const char* fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+static int cuda_fail(cudaError_t e, const char* what)
+{
+    return fail(DSV41_E_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+int num_sms()
+{
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ------------------------------------------------------------------------------------------
+// workspace layout
+// ------------------------------------------------------------------------------------------
+struct Layout {
+    size_t status, counts, offsets, token_sorted, weight_sorted, route_sorted, expert_sorted, route_pos, groups,
+        nlists, fat_experts, seg_hist, xt_g, xt_u, xt_d, y, partials, counters, gemm, total;
+    int N, E, H, I, split, groups_bound, units_bound;
+};
+
+static int auto_split(int N, int E, int H, int I, int requested)
+{
+    auto fits = [&](int s) { return s >= 1 && (H / 16) % (s * 8) == 0 && (I / 16) % (s * 8) == 0; };
+    if (requested > 0) return fits(requested) ? requested : 1;
+    const int groups = N < E ? (N > 0 ? N : 1) : E;
+    const long long units = (long long)groups * (I / 128);
+    const long long target = 2LL * num_sms();
+    int s = 1;
+    while (units * s < target && s < 8 && fits(s * 2)) s *= 2;
+    return s;
+}
+
+static Layout make_layout(int T, int topk, int E, int H, int I, int split_req, int fat)
+{
+    Layout L{};
+    L.N = T * topk;
+    L.E = E;
+    L.H = H;
+    L.I = I;
+    L.split = auto_split(L.N, E, H, I, split_req);
+    L.groups_bound = max_groups(L.N, E);
+    L.units_bound = gemv_units_alloc(L.groups_bound, H, I, L.split);
+    const size_t N = (size_t)(L.N > 0 ? L.N : 1), E1 = (size_t)E + 1;
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = align_up(o + bytes, 256);
+        return at;
+    };
+    L.status = take(256);
+    L.counts = take(E1 * 4);
+    L.offsets = take(E1 * 4);
+    L.token_sorted = take(N * 4);
+    L.weight_sorted = take(N * 4);
+    L.route_sorted = take(N * 4);
+    L.expert_sorted = take(N * 4);
+    L.route_pos = take(N * 4);
+    L.groups = take((size_t)L.groups_bound * 16);
+    L.nlists = take(16);
+    L.fat_experts = take(E1 * 4);
+    L.seg_hist = take(perm_seg_hist_ints(L.N, E) * 4 + 4);
+    L.xt_g = take(N * H * 2);
+    L.xt_u = take(N * H * 2);
+    L.xt_d = take(N * I * 2);
+    L.y = take(N * H * 2);
+    L.partials = take(L.split > 1 ? (size_t)L.units_bound * 4096 * 4 : 16);
+    L.counters = take((size_t)(L.units_bound / L.split + 1) * 4);
+    L.gemm = take(fat >= 0 ? gemm_scratch_bytes(L.N, E, H, I) : 16);
+    L.total = o;
+    return L;
+}
+
+template <typename T>
+static T* at(void* ws, size_t off)
+{
+    return reinterpret_cast<T*>(static_cast<uint8_t*>(ws) + off);
+}
+
+static PermBuffers perm_buffers(void* ws, const Layout& L)
+{
+    PermBuffers pb{};
+    pb.counts = at<int>(ws, L.counts);
+    pb.offsets = at<int>(ws, L.offsets);
+    pb.token_sorted = at<int>(ws, L.token_sorted);
+    pb.weight_sorted = at<float>(ws, L.weight_sorted);
+    pb.route_sorted = at<int>(ws, L.route_sorted);
+    pb.expert_sorted = at<int>(ws, L.expert_sorted);
+    pb.route_pos = at<int>(ws, L.route_pos);
+    pb.groups = at<int4>(ws, L.groups);
+    pb.n_groups = at<int>(ws, L.nlists);
+    pb.n_fat = at<int>(ws, L.nlists) + 1;
+    pb.fat_experts = at<int>(ws, L.fat_experts);
+    pb.seg_hist = at<int>(ws, L.seg_hist);
+    return pb;
+}
+
+constexpr int kExpertGemmFat = -1;  // busy experts use the GEMV groups until the tcgen05 GEMM is enabled
+
+static int check_layer(const dsv41_moe_layer* layer)
+{
+    if (!layer) return fail(DSV41_E_INVALID, "layer is NULL");
+    const int E = layer->num_experts, H = layer->hidden, I = layer->intermediate;
+    if (E <= 0 || E > kMaxExperts) return fail(DSV41_E_INVALID, "num_experts %d out of range (1..%d)", E, kMaxExperts);
+    if (H <= 0 || I <= 0 || H % 256 || I % 256)
+        return fail(DSV41_E_INVALID, "hidden %d / intermediate %d must be positive multiples of 256", H, I);
+    if (!layer->gate_ptrs || !layer->up_ptrs || !layer->down_ptrs || !layer->w13_suh || !layer->w13_svh ||
+        !layer->w2_suh || !layer->w2_svh)
+        return fail(DSV41_E_INVALID, "layer has a NULL tensor pointer");
+    return DSV41_OK;
+}
+
+// gate/up pass (GEMV groups, then GEMM for fat experts) and down pass over prepared rows
+static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuffers& pb, __half* xt_g, __half* xt_u,
+                                     __half* xt_d, __half* y, float* partials, int* counters, int* status, int split,
+                                     int groups_bound, int rows_bound, float limit, int fat, uint8_t* gemm_scratch,
+                                     cudaStream_t st)
+{
+    const int H = layer->hidden, I = layer->intermediate;
+    cudaError_t err;
+    if (split > 1) {
+        const size_t n = (size_t)(gemv_units_alloc(groups_bound, H, I, split) / split + 1) * 4;
+        if ((err = cudaMemsetAsync(counters, 0, n, st)) != cudaSuccess) return err;
+    }
+    GemmArgs ga{};
+    ga.layer = layer;
+    ga.fat_experts = pb.fat_experts;
+    ga.n_fat = pb.n_fat;
+    ga.counts = pb.counts;
+    ga.offsets = pb.offsets;
+    ga.xt_g = xt_g;
+    ga.xt_u = xt_u;
+    ga.xt_d = xt_d;
+    ga.y = y;
+    ga.rows_bound = rows_bound;
+    ga.limit = limit;
+    ga.scratch = gemm_scratch;
+    ga.status = status;
+    GemvParams gp{};
+    gp.groups = pb.groups;
+    gp.n_groups = pb.n_groups;
+    gp.partials = partials;
+    gp.counters = counters;
+    gp.status = status;
+    gp.split = split;
+    gp.limit = limit;
+    gp.tab_a = layer->gate_ptrs;
+    gp.tab_b = layer->up_ptrs;
+    gp.xa = xt_g;
+    gp.xb = xt_u;
+    gp.svh_a = static_cast<const __half*>(layer->w13_svh);
+    gp.suh_d = static_cast<const __half*>(layer->w2_suh);
+    gp.out = xt_d;
+    gp.K = H;
+    gp.N = I;
+    if ((err = launch_gemv(0, gp, gemv_units_bound(groups_bound, H, I, 0, split), st)) != cudaSuccess) return err;
+    if (fat >= 0 && (err = launch_gemm_gateup(ga, st)) != cudaSuccess) return err;
+    gp.tab_a = layer->down_ptrs;
+    gp.tab_b = nullptr;
+    gp.xa = xt_d;
+    gp.xb = nullptr;
+    gp.svh_a = static_cast<const __half*>(layer->w2_svh);
+    gp.suh_d = nullptr;
+    gp.out = y;
+    gp.K = I;
+    gp.N = H;
+    if ((err = launch_gemv(1, gp, gemv_units_bound(groups_bound, I, H, 1, split), st)) != cudaSuccess) return err;
+    if (fat >= 0 && (err = launch_gemm_down(ga, st)) != cudaSuccess) return err;
+    return cudaSuccess;
+}
+
+}  // namespace dsv41
+
+using namespace dsv41;
+
+extern "C" {
+
+const char* dsv41_last_error(void) { return g_last_error.c_str(); }
+
+int dsv41_abi_version(void) { return DSV41_ABI_VERSION; }
+
+const char* dsv41_build_info(void)
+{
+    return "dsv41_b200: sm_100a; EXL3 mul1 K=3; decode-GEMV mma.m16n8k16 (register-decoded B), "
+           "tcgen05 grouped GEMM; nvcc " DSV41_NVCC_VERSION;
+}
+
+int dsv41_moe_workspace_size(int32_t T, int32_t topk, int32_t num_experts, int32_t hidden, int32_t intermediate,
+                             const dsv41_moe_options* opt, size_t* bytes)
+{
+    if (!bytes) return fail(DSV41_E_INVALID, "bytes is NULL");
+    if (T < 0 || topk <= 0 || num_experts <= 0 || num_experts > kMaxExperts || hidden <= 0 || intermediate <= 0 ||
+        hidden % 256 || intermediate % 256)
+        return fail(DSV41_E_INVALID, "bad sizes T=%d topk=%d E=%d H=%d I=%d", T, topk, num_experts, hidden,
+                    intermediate);
+    const int split = opt ? opt->split_k : 0;
+    const int fat = opt ? opt->fat_threshold : -1;
+    *bytes = make_layout(T, topk, num_experts, hidden, intermediate, split, fat).total;
+    return DSV41_OK;
+}
+
+int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dtype, int32_t T, const int64_t* ids,
+                      const float* weights, int32_t topk, const dsv41_moe_options* opt, float* out, void* workspace,
+                      size_t workspace_bytes, void* stream)
+{
+    int rc = check_layer(layer);
+    if (rc) return rc;
+    if (T < 0 || topk <= 0) return fail(DSV41_E_INVALID, "bad T=%d topk=%d", T, topk);
+    if (x_dtype < DSV41_DTYPE_F16 || x_dtype > DSV41_DTYPE_F32) return fail(DSV41_E_INVALID, "bad x_dtype %d", x_dtype);
+    if (T > 0 && (!x || !ids || !weights || !out)) return fail(DSV41_E_INVALID, "NULL input/output pointer");
+    if (!workspace) return fail(DSV41_E_INVALID, "workspace is NULL");
+    const int E = layer->num_experts, H = layer->hidden, I = layer->intermediate;
+    const dsv41_moe_options dflt{-1, 0.0f, nullptr, 0, 0};
+    const dsv41_moe_options& o = opt ? *opt : dflt;
+    if (o.expert_map && o.map_len <= 0) return fail(DSV41_E_INVALID, "expert_map given with map_len %d", o.map_len);
+    const Layout L = make_layout(T, topk, E, H, I, o.split_k, o.fat_threshold);
+    if (workspace_bytes < L.total)
+        return fail(DSV41_E_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, L.total);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (T == 0) return DSV41_OK;
+    cudaError_t err;
+    const PermBuffers pb = perm_buffers(workspace, L);
+    int* status = at<int>(workspace, L.status);
+    if ((err = launch_permute(ids, weights, L.N, topk, E, o.expert_map, o.map_len, o.fat_threshold, pb, st)) !=
+        cudaSuccess)
+        return cuda_fail(err, "permute");
+    __half* xt_g = at<__half>(workspace, L.xt_g);
+    __half* xt_u = at<__half>(workspace, L.xt_u);
+    __half* xt_d = at<__half>(workspace, L.xt_d);
+    __half* y = at<__half>(workspace, L.y);
+    if ((err = launch_prep(x, x_dtype, pb.token_sorted, pb.expert_sorted, pb.offsets + E, L.N,
+                           static_cast<const __half*>(layer->w13_suh), H, xt_g, xt_u, st)) != cudaSuccess)
+        return cuda_fail(err, "prep");
+    if ((err = run_expert_passes(layer, pb, xt_g, xt_u, xt_d, y, at<float>(workspace, L.partials),
+                                 at<int>(workspace, L.counters), status, L.split, L.groups_bound, L.N, o.limit,
+                                 o.fat_threshold, at<uint8_t>(workspace, L.gemm), st)) != cudaSuccess)
+        return cuda_fail(err, "expert passes");
+    if ((err = launch_combine(y, pb.route_pos, weights, T, topk, H, 0, out, st)) != cudaSuccess)
+        return cuda_fail(err, "combine");
+    return DSV41_OK;
+}
+
+size_t dsv41_permute_workspace_size(int32_t T, int32_t topk, int32_t num_experts)
+{
+    const int N = T * topk;
+    const size_t E1 = (size_t)num_experts + 1, n = (size_t)(N > 0 ? N : 1);
+    // counts, offsets, token/weight/route/expert sorted, route_pos, groups, lists, fat, seg_hist
+    return align_up(E1 * 4, 256) * 3 + align_up(n * 4, 256) * 5 + align_up((size_t)max_groups(N, num_experts) * 16, 256) +
+           256 + align_up(perm_seg_hist_ints(N, num_experts) * 4 + 4, 256) + 4096;
+}
+
+int dsv41_permute(const int64_t* ids, const float* weights, int32_t T, int32_t topk, int32_t num_experts,
+                  const int32_t* expert_map, int32_t map_len, int64_t* counts, int64_t* offsets, int32_t* token_sorted,
+                  float* weight_sorted, int32_t* route_sorted, int32_t* route_pos, void* workspace,
+                  size_t workspace_bytes, void* stream)
+{
+    if (T < 0 || topk <= 0 || num_experts <= 0 || num_experts > kMaxExperts)
+        return fail(DSV41_E_INVALID, "bad sizes T=%d topk=%d E=%d", T, topk, num_experts);
+    if (T > 0 && !ids) return fail(DSV41_E_INVALID, "ids is NULL");
+    if (expert_map && map_len <= 0) return fail(DSV41_E_INVALID, "expert_map given with map_len %d", map_len);
+    if (!workspace || workspace_bytes < dsv41_permute_workspace_size(T, topk, num_experts))
+        return fail(DSV41_E_WORKSPACE, "permute workspace too small");
+    const int N = T * topk;
+    const size_t E1 = (size_t)num_experts + 1, n = (size_t)(N > 0 ? N : 1);
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t a = o;
+        o = align_up(o + bytes, 256);
+        return a;
+    };
+    PermBuffers pb{};
+    pb.counts = at<int>(workspace, take(E1 * 4));
+    pb.offsets = at<int>(workspace, take(E1 * 4));
+    pb.fat_experts = at<int>(workspace, take(E1 * 4));
+    pb.token_sorted = token_sorted ? token_sorted : at<int>(workspace, take(n * 4));
+    pb.weight_sorted = weight_sorted ? weight_sorted : at<float>(workspace, take(n * 4));
+    pb.route_sorted = route_sorted ? route_sorted : at<int>(workspace, take(n * 4));
+    pb.expert_sorted = at<int>(workspace, take(n * 4));
+    pb.route_pos = route_pos ? route_pos : at<int>(workspace, take(n * 4));
+    pb.groups = at<int4>(workspace, take((size_t)max_groups(N, num_experts) * 16));
+    pb.n_groups = at<int>(workspace, take(16));
+    pb.n_fat = pb.n_groups + 1;
+    pb.seg_hist = at<int>(workspace, take(perm_seg_hist_ints(N, num_experts) * 4 + 4));
+    pb.counts64 = counts;
+    pb.offsets64 = offsets;
+    cudaError_t err = launch_permute(ids, weights, N, topk, num_experts, expert_map, map_len, -1, pb,
+                                     static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "permute");
+    return DSV41_OK;
+}
+
+int dsv41_combine(const void* y, const int32_t* route_pos, const float* weights, int32_t T, int32_t topk,
+                  int32_t hidden, int32_t accumulate, float* out, void* stream)
+{
+    if (T < 0 || topk <= 0 || hidden <= 0 || hidden % 8) return fail(DSV41_E_INVALID, "bad sizes");
+    if (T == 0) return DSV41_OK;
+    if (!y || !route_pos || !weights || !out) return fail(DSV41_E_INVALID, "NULL pointer");
+    cudaError_t err = launch_combine(static_cast<const __half*>(y), route_pos, weights, T, topk, hidden, accumulate, out,
+                                     static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "combine");
+    return DSV41_OK;
+}
+
+int dsv41_decode_dense(const void* trellis, int32_t k, int32_t n, void* w_out, void* stream)
+{
+    if (k <= 0 || n <= 0 || k % 16 || n % 16) return fail(DSV41_E_INVALID, "k=%d n=%d must be multiples of 16", k, n);
+    if (!trellis || !w_out) return fail(DSV41_E_INVALID, "NULL pointer");
+    if (reinterpret_cast<uintptr_t>(trellis) % 4) return fail(DSV41_E_INVALID, "trellis must be 4-byte aligned");
+    cudaError_t err = launch_decode_dense(trellis, k, n, static_cast<__half*>(w_out), static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "decode_dense");
+    return DSV41_OK;
+}
+
+static size_t expert_gemm_layout(int R, int n_experts, int H, int I, size_t* offs)
+{
+    const size_t E1 = (size_t)kMaxExperts + 1, n = (size_t)(R > 0 ? R : 1);
+    const int split = auto_split(R, n_experts > 0 ? n_experts : 1, H, I, 0);
+    const int gb = max_groups(R, n_experts > 0 ? n_experts : 1);
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t a = o;
+        o = align_up(o + bytes, 256);
+        return a;
+    };
+    offs[0] = take(256);                      // status
+    offs[1] = take(E1 * 4);                   // counts32
+    offs[2] = take(E1 * 4);                   // offsets32
+    offs[3] = take(E1 * 4);                   // fat list
+    offs[4] = take(n * 4);                    // expert_sorted
+    offs[5] = take((size_t)gb * 16);          // groups
+    offs[6] = take(16);                       // n_groups, n_fat, nrows
+    offs[7] = take(n * H * 2);                // xt_g
+    offs[8] = take(n * H * 2);                // xt_u
+    offs[9] = take(n * I * 2);                // xt_d
+    offs[10] = take(n * H * 2);               // y
+    offs[11] = take(split > 1 ? (size_t)gemv_units_alloc(gb, H, I, split) * 4096 * 4 : 16);
+    offs[12] = take((size_t)(gemv_units_alloc(gb, H, I, split) / split + 1) * 4);
+    offs[13] = take(gemm_scratch_bytes(R, n_experts, H, I));
+    offs[14] = (size_t)split;
+    offs[15] = (size_t)gb;
+    return o;
+}
+
+int dsv41_expert_gemm_workspace_size(int32_t total_rows, int32_t n_experts, int32_t hidden, int32_t intermediate,
+                                     size_t* bytes)
+{
+    if (!bytes || total_rows < 0 || n_experts < 0 || n_experts > kMaxExperts || hidden <= 0 || intermediate <= 0 ||
+        hidden % 256 || intermediate % 256)
+        return fail(DSV41_E_INVALID, "bad sizes rows=%d n=%d H=%d I=%d", total_rows, n_experts, hidden, intermediate);
+    size_t offs[16];
+    *bytes = expert_gemm_layout(total_rows, n_experts, hidden, intermediate, offs);
+    return DSV41_OK;
+}
+
+int dsv41_expert_gemm(const dsv41_moe_layer* layer, const void* x, int32_t x_dtype, int32_t T, const int32_t* experts,
+                      int32_t n_experts, const int64_t* counts, const int64_t* offsets, const int32_t* token_sorted,
+                      const float* weight_sorted, int32_t total_rows, float limit, float* out, void* workspace,
+                      size_t workspace_bytes, void* stream)
+{
+    int rc = check_layer(layer);
+    if (rc) return rc;
+    if (x_dtype < DSV41_DTYPE_F16 || x_dtype > DSV41_DTYPE_F32) return fail(DSV41_E_INVALID, "bad x_dtype %d", x_dtype);
+    if (n_experts < 0 || n_experts > layer->num_experts || total_rows < 0 || T < 0)
+        return fail(DSV41_E_INVALID, "bad sizes n_experts=%d total_rows=%d T=%d", n_experts, total_rows, T);
+    if (n_experts == 0 || total_rows == 0) return DSV41_OK;
+    if (!x || !experts || !counts || !offsets || !token_sorted || !weight_sorted || !out || !workspace)
+        return fail(DSV41_E_INVALID, "NULL pointer");
+    const int H = layer->hidden, I = layer->intermediate, E = layer->num_experts;
+    size_t offs[16];
+    const size_t need = expert_gemm_layout(total_rows, n_experts, H, I, offs);
+    if (workspace_bytes < need) return fail(DSV41_E_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, need);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int split = (int)offs[14], gb = (int)offs[15];
+    const int fat = kExpertGemmFat;
+    PermBuffers pb{};
+    pb.counts = at<int>(workspace, offs[1]);
+    pb.offsets = at<int>(workspace, offs[2]);
+    pb.fat_experts = at<int>(workspace, offs[3]);
+    pb.expert_sorted = at<int>(workspace, offs[4]);
+    pb.groups = at<int4>(workspace, offs[5]);
+    pb.n_groups = at<int>(workspace, offs[6]);
+    pb.n_fat = pb.n_groups + 1;
+    int* nrows = pb.n_groups + 2;
+    pb.token_sorted = const_cast<int*>(token_sorted);
+    pb.weight_sorted = const_cast<float*>(weight_sorted);
+    cudaError_t err;
+    if ((err = launch_list_setup(experts, n_experts, counts, offsets, E, total_rows, fat, pb, nrows, st)) != cudaSuccess)
+        return cuda_fail(err, "list setup");
+    __half* xt_g = at<__half>(workspace, offs[7]);
+    __half* xt_u = at<__half>(workspace, offs[8]);
+    __half* xt_d = at<__half>(workspace, offs[9]);
+    __half* y = at<__half>(workspace, offs[10]);
+    if ((err = launch_prep(x, x_dtype, token_sorted, pb.expert_sorted, nrows, total_rows,
+                           static_cast<const __half*>(layer->w13_suh), H, xt_g, xt_u, st)) != cudaSuccess)
+        return cuda_fail(err, "prep");
+    if ((err = run_expert_passes(layer, pb, xt_g, xt_u, xt_d, y, at<float>(workspace, offs[11]),
+                                 at<int>(workspace, offs[12]), at<int>(workspace, offs[0]), split, gb, total_rows, limit,
+                                 fat, at<uint8_t>(workspace, offs[13]), st)) != cudaSuccess)
+        return cuda_fail(err, "expert passes");
+    if ((err = launch_scatter_add(y, experts, n_experts, pb.counts, pb.offsets, token_sorted, weight_sorted, H, total_rows,
+                                  out, st)) != cudaSuccess)
+        return cuda_fail(err, "scatter add");
+    return DSV41_OK;
+}
+
+int dsv41_read_status(const void* workspace, void* stream, int32_t* status)
+{
+    if (!workspace || !status) return fail(DSV41_E_INVALID, "NULL pointer");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t err = cudaStreamSynchronize(st);
+    if (err != cudaSuccess) return cuda_fail(err, "synchronize");
+    int v = 0;
+    if ((err = cudaMemcpy(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(err, "read status");
+    if (v && (err = cudaMemset(const_cast<void*>(workspace), 0, sizeof(int))) != cudaSuccess)
+        return cuda_fail(err, "clear status");
+    *status = v;
+    return DSV41_OK;
+}
+
+}  // extern "C"

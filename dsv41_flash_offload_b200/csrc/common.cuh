@@ -1,0 +1,225 @@
+// Shared device helpers for the EXL3 mul1 K=3 MoE kernels (sm_100a).
+//
+// Format (restated from the reference's kernels/cpu_avx2/ft_core.h:28-83, which mirrors
+// exllamav3's GPU decode): a 16x16 weight tile is a circular 768-bit stream (96 bytes = 24
+// little-endian 32-bit words, read MSB-first). Symbol i's 16-bit state is the stream window
+// ending at bit 3i+2; its weight is fp16(fma(1024 + bytesum(state * 0x83DCD12D), KINV, KBIAS)).
+// Symbols 8t..8t+7 belong to tensor-core fragment lane t, laid out exactly as the B operand of
+// mma.m16n8k16 (rows k = 2(t%4)+{0,1,8,9}, cols n = t/4 and t/4+8), so each lane decodes its own
+// B fragments in registers and the decoded weights never touch memory.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dsv41 {
+
+constexpr uint32_t kMul1 = 0x83DCD12Du;
+constexpr float kHad = 0.088388347648f;  // 2^-3.5
+constexpr int kTileBytes = 96;
+constexpr int kTileWords = 24;
+constexpr uint16_t kKinvBits = 0x1eee;
+constexpr uint16_t kKbiasBits = 0xc931;
+
+// status word codes written by kernels (never a trap)
+enum : int { kStatusOk = 0, kStatusWaitTimeout = 1, kStatusBadShape = 2 };
+
+// ------------------------------------------------------------------------------------------
+// decode
+// ------------------------------------------------------------------------------------------
+struct LaneDecode {
+    int w_hi, w_lo;  // word indices of this lane's 64-bit window inside the tile
+    uint32_t pre;    // pre-shift (0 or 16) that brings every state below bit 32 of the window
+    int base;        // shift of symbol 0; symbol j is at base - 3j
+};
+
+// Lane t's 8 states span stream bits [24t-13, 24t+24). With o = start % 32 that window fits in
+// words (a, a+1); lanes with o < 16 shift the pair right by 16 first so all 8 shifts are < 32.
+__device__ __forceinline__ LaneDecode lane_decode_setup(int t)
+{
+    const int start = (24 * t - 13 + 768) % 768;
+    const int a = start >> 5, o = start & 31;
+    LaneDecode d;
+    d.w_hi = a;
+    d.w_lo = (a + 1) % kTileWords;
+    if (o < 16) { d.pre = 16; d.base = 32 - o; }
+    else { d.pre = 0; d.base = 48 - o; }
+    return d;
+}
+
+__device__ __forceinline__ __half2 u32_as_half2(uint32_t v)
+{
+    __half2 h;
+    *reinterpret_cast<uint32_t*>(&h) = v;
+    return h;
+}
+__device__ __forceinline__ uint32_t half2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// one state -> 0x6400 + bytesum(state * MUL1) = the fp16 bit pattern of (1024 + s) (s <= 1020)
+__device__ __forceinline__ uint32_t state_code(uint32_t st)
+{
+    return __dp4a(st * kMul1, 0x01010101u, 0x6400u);
+}
+
+// Decode this lane's 8 symbols of one tile (its two window words) into 4 half2 registers in
+// mma B-fragment order: b[0] = (k r0, r0+1 | n c0), b[1] = (r0+8, r0+9 | c0), b[2], b[3] same
+// for column c0+8. One fp16 rounding per weight (HFMA2), bit-exact with the reference decode.
+__device__ __forceinline__ void decode_lane(uint32_t whi, uint32_t wlo, const LaneDecode& d, uint32_t (&b)[4])
+{
+    const uint32_t lo = __funnelshift_r(wlo, whi, d.pre);
+    const uint32_t hi = whi >> d.pre;
+    const __half2 kinv = u32_as_half2((uint32_t)kKinvBits * 0x10001u);
+    const __half2 kbias = u32_as_half2((uint32_t)kKbiasBits * 0x10001u);
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+        const uint32_t s0 = __funnelshift_r(lo, hi, d.base - 3 * j) & 0xffffu;
+        const uint32_t s1 = __funnelshift_r(lo, hi, d.base - 3 * (j + 1)) & 0xffffu;
+        const uint32_t c = __byte_perm(state_code(s0), state_code(s1), 0x5410);
+        b[j >> 1] = half2_as_u32(__hfma2(u32_as_half2(c), kinv, kbias));
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// fp16 rounding helper and the 128-point Walsh-Hadamard transform over a warp
+// (lane holds elements lane*4 + q, q = 0..3; stage order w = 1, 2, 4, ..., 64 as the reference's
+// had128, ft_core.h:89-94, so every fp32 intermediate is the same)
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ float r16(float f) { return __half2float(__float2half_rn(f)); }
+
+__device__ __forceinline__ void had128_warp(float (&v)[4], int lane)
+{
+    float a = v[0], b = v[1];
+    v[0] = a + b; v[1] = a - b;
+    a = v[2]; b = v[3];
+    v[2] = a + b; v[3] = a - b;
+    a = v[0]; b = v[2];
+    v[0] = a + b; v[2] = a - b;
+    a = v[1]; b = v[3];
+    v[1] = a + b; v[3] = a - b;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+        const bool upper = (lane & m) != 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float p = __shfl_xor_sync(0xffffffffu, v[q], m);
+            v[q] = upper ? (p - v[q]) : (v[q] + p);
+        }
+    }
+}
+
+// silu(g) with the reference's clamp (u to [-L, L], silu from above; L = 0 disables),
+// ft_core.h:123-133
+__device__ __forceinline__ float act_gu(float g, float u, float limit)
+{
+    float s = g / (1.0f + expf(-g));
+    if (limit != 0.0f) {
+        u = fminf(fmaxf(u, -limit), limit);
+        s = fminf(s, limit);
+    }
+    return __fmul_rn(s, u);
+}
+
+// ------------------------------------------------------------------------------------------
+// async copy / mbarrier primitives (bounded waits: a wait that runs out records a status code
+// and returns false; it never traps)
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s, as the reference's combine wait
+
+// Wait for phase `parity` of `bar`. Returns false (and records kStatusWaitTimeout) if it has
+// not completed within kWaitLimitNs or if `abort_flag` is already set.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                *abort_flag = 1;
+                if (status) atomicExch(status, kStatusWaitTimeout);
+                return false;
+            }
+        }
+    }
+}
+
+// 1-D bulk async copy global -> shared, completing on an mbarrier (no multicast)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&a)[4], uint32_t addr)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+}  // namespace dsv41

@@ -1,0 +1,278 @@
+// Fused decode-GEMV for experts with few rows (decode steps; the GEMV share of prefill).
+//
+// Replaces the grouped per-expert decode/GEMV of exllamav3_ext.exl3_moe as launched by
+// apply_exl3_fused_moe (patches/vllm-exl3-host-dma.patch:315-449), restating the math of the
+// reference CPU tier (kernels/cpu_avx2/ft_core.h:587-727 moe_forward phases, :994-1011 ref_*):
+//   pass 0 (gate/up): y_g, y_u = xt_{g,u} . W_{g,u}; out_block each 128 block; a = fp16(act);
+//                     xt_d = prep_block(a, suh_d)              -> xt_d [rows][I] fp16
+//   pass 1 (down):    y = out_block(xt_d . W_d)                -> y    [rows][H] fp16
+//
+// Work unit = (row group of <= 16 rows of one expert, column block, K split). A persistent grid
+// of 2 CTAs per SM walks the units. Per CTA: 16 consumer warps + 1 producer warp.
+//   producer: one 1-D bulk async copy (cp.async.bulk, no multicast) per 768/1536-byte trellis
+//             k-row segment and per 256-byte activation row into a 4-stage mbarrier ring;
+//             trellis reads carry an L2 evict-first hint (each expert byte is read once).
+//   consumer warp w: owns one 16-column n-tile; per k-tile it loads the two 32-bit window
+//             words of its lane from the staged tile, decodes its 8 weights into two mma B
+//             fragments in registers, and issues two mma.m16n8k16 (rows = tokens) against the
+//             ldmatrix'd activations. Decoded weights never leave registers.
+// Split-K partials (small batches) are reduced in a fixed order by the last-arriving CTA, so
+// results are deterministic.
+#include "common.cuh"
+#include "internal.h"
+
+namespace dsv41 {
+
+constexpr int kConsumerWarps = 16;
+constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStageRows = 8;          // k-tile rows per stage
+constexpr int kStages = 4;
+constexpr int kRowBytes = 1536;        // 16 tiles of one k-row
+constexpr int kXRowStride = 272;       // 8 k-tiles x 16 halves = 256 B, + 16 B pad (ldmatrix banks)
+constexpr int kXMatBytes = 16 * kXRowStride;
+constexpr int kEpFloats = 4096;
+
+struct GemvSmem {
+    uint8_t tr[kStages][kStageRows * kRowBytes];
+    uint8_t x[kStages][2][kXMatBytes];
+    float ep[kEpFloats];
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    int abort_flag;
+    int last_flag;
+};
+
+size_t gemv_smem_bytes() { return sizeof(GemvSmem); }
+
+__device__ __forceinline__ void out_block4(float (&y)[4], const __half* svh, int lane)
+{
+#pragma unroll
+    for (int q = 0; q < 4; ++q) y[q] = r16(y[q]);
+    had128_warp(y, lane);
+    const uint2 u = *reinterpret_cast<const uint2*>(svh);
+    const __half2 a = u32_as_half2(u.x), b = u32_as_half2(u.y);
+    const float s[4] = {__low2float(a), __high2float(a), __low2float(b), __high2float(b)};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) y[q] = r16(__fmul_rn(__fmul_rn(y[q], kHad), s[q]));
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kGemvThreads, 2) exl3_gemv_kernel(const GemvParams p)
+{
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    GemvSmem& S = *reinterpret_cast<GemvSmem*>(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int nmat = MODE == 0 ? 2 : 1;
+    constexpr int cols = MODE == 0 ? 128 : 256;
+    const int ktiles = p.K / 16;
+    const int n_cb = p.N / cols;
+    const int k_per_split = ktiles / p.split;
+    const int stages_per_unit = k_per_split / kStageRows;
+    const int n_units = (*p.n_groups) * n_cb * p.split;
+    const int ntile_row = p.N / 16;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&S.full[s], 1);
+            mbar_init(&S.empty[s], kConsumerWarps);
+        }
+        S.abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------ producer warp ------------------------------
+        const uint64_t pol_w = l2_policy_evict_first();
+        const uint64_t pol_x = l2_policy_evict_last();
+        uint32_t it = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            const int s = u % p.split, ucb = u / p.split, cb = ucb % n_cb, g = ucb / n_cb;
+            const int4 G = p.groups[g];
+            const int e = G.x, row0 = G.y, rows = G.z;
+            const uint8_t* ta = reinterpret_cast<const uint8_t*>(p.tab_a[e]);
+            const uint8_t* tb = MODE == 0 ? reinterpret_cast<const uint8_t*>(p.tab_b[e]) : nullptr;
+            for (int st = 0; st < stages_per_unit; ++st, ++it) {
+                const int stage = it % kStages;
+                const uint32_t round = it / kStages;
+                if (!mbar_wait_bounded(&S.empty[stage], (round & 1) ^ 1, &S.abort_flag, p.status)) {
+                    ok = false;
+                    break;
+                }
+                const int kt0 = s * k_per_split + st * kStageRows;
+                if (lane == 0) mbar_arrive_expect_tx(&S.full[stage], kStageRows * kRowBytes + nmat * rows * 256);
+                __syncwarp();
+                if (MODE == 0) {
+                    if (lane < 2 * kStageRows) {
+                        const int r = lane >> 1, which = lane & 1;
+                        const uint8_t* src = (which ? tb : ta) + ((size_t)(kt0 + r) * ntile_row + cb * 8) * kTileBytes;
+                        bulk_g2s(S.tr[stage] + r * kRowBytes + which * 768, src, 768, &S.full[stage], pol_w);
+                    }
+                } else {
+                    if (lane < kStageRows) {
+                        const uint8_t* src = ta + ((size_t)(kt0 + lane) * ntile_row + cb * 16) * kTileBytes;
+                        bulk_g2s(S.tr[stage] + lane * kRowBytes, src, kRowBytes, &S.full[stage], pol_w);
+                    }
+                }
+                for (int c = lane; c < nmat * rows; c += 32) {
+                    const int m = c / rows, j = c % rows;
+                    const __half* src = (m ? p.xb : p.xa) + (size_t)(row0 + j) * p.K + kt0 * 16;
+                    bulk_g2s(S.x[stage][m] + j * kXRowStride, src, 256, &S.full[stage], pol_x);
+                }
+            }
+        }
+        if (!ok && lane == 0) {
+            // drain: do not leave the CTA while copies into its shared memory are in flight
+            const uint32_t n_back = it < (uint32_t)kStages ? it : (uint32_t)kStages;
+            for (uint32_t q = 1; q <= n_back; ++q) {
+                const uint32_t j = it - q;
+                const uint64_t t0 = globaltimer_ns();
+                while (!mbar_try_wait(&S.full[j % kStages], (j / kStages) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {}
+            }
+        }
+        return;
+    }
+
+    // ------------------------------ consumer warps ------------------------------
+    const LaneDecode ld = lane_decode_setup(lane);
+    const int mat = MODE == 0 ? (warp >> 3) : 0;
+    const int tile_in_row = warp;  // byte offset warp * 96 inside a staged 1536-byte k-row
+    const uint32_t x_lane = ((lane & 7) + ((lane >> 3) & 1) * 8) * kXRowStride + ((lane >> 4) & 1) * 16;
+    uint32_t it = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const int ucb = u / p.split, cb = ucb % n_cb, g = ucb / n_cb;
+        const int4 G = p.groups[g];
+        const int e = G.x, row0 = G.y, rows = G.z;
+        float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int st = 0; st < stages_per_unit; ++st, ++it) {
+            const int stage = it % kStages;
+            const uint32_t round = it / kStages;
+            mbar_wait_bounded(&S.full[stage], round & 1, &S.abort_flag, p.status);
+            const uint32_t* trow = reinterpret_cast<const uint32_t*>(S.tr[stage]) + tile_in_row * kTileWords;
+            const uint32_t xaddr = smem_addr(S.x[stage][mat]) + x_lane;
+#pragma unroll
+            for (int r = 0; r < kStageRows; ++r) {
+                const uint32_t* tw = trow + r * (kRowBytes / 4);
+                uint32_t b[4];
+                decode_lane(tw[ld.w_hi], tw[ld.w_lo], ld, b);
+                uint32_t a[4];
+                ldmatrix_x4(a, xaddr + r * 32);
+                mma_16816(acc0, a, b[0], b[1]);
+                mma_16816(acc1, a, b[2], b[3]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.empty[stage]);
+        }
+
+        // accumulators -> shared [mat][row][cols]
+        {
+            const int tcol = (MODE == 0 ? (warp & 7) : warp) * 16 + (lane & 3) * 2;
+            const int r = lane >> 2;
+            float* ep = S.ep + (MODE == 0 ? mat * 16 * cols : 0);
+            *reinterpret_cast<float2*>(ep + r * cols + tcol) = make_float2(acc0[0], acc0[1]);
+            *reinterpret_cast<float2*>(ep + (r + 8) * cols + tcol) = make_float2(acc0[2], acc0[3]);
+            *reinterpret_cast<float2*>(ep + r * cols + tcol + 8) = make_float2(acc1[0], acc1[1]);
+            *reinterpret_cast<float2*>(ep + (r + 8) * cols + tcol + 8) = make_float2(acc1[2], acc1[3]);
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+
+        if (p.split > 1) {
+            float* slot = p.partials + (size_t)u * kEpFloats;
+            for (int i = threadIdx.x * 4; i < kEpFloats; i += kConsumerWarps * 32 * 4)
+                __stcg(reinterpret_cast<float4*>(slot + i), *reinterpret_cast<const float4*>(S.ep + i));
+            __threadfence();
+            named_bar_sync(1, kConsumerWarps * 32);
+            if (threadIdx.x == 0) {
+                const int old = atomicAdd(p.counters + ucb, 1);
+                S.last_flag = (old == p.split - 1);
+            }
+            named_bar_sync(1, kConsumerWarps * 32);
+            if (!S.last_flag) continue;
+            __threadfence();
+            for (int i = threadIdx.x * 4; i < kEpFloats; i += kConsumerWarps * 32 * 4) {
+                float4 v = __ldcg(reinterpret_cast<const float4*>(p.partials + (size_t)ucb * p.split * kEpFloats + i));
+                for (int s2 = 1; s2 < p.split; ++s2) {
+                    const float4 w = __ldcg(reinterpret_cast<const float4*>(
+                        p.partials + ((size_t)ucb * p.split + s2) * kEpFloats + i));
+                    v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+                }
+                *reinterpret_cast<float4*>(S.ep + i) = v;
+            }
+            if (threadIdx.x == 0) p.counters[ucb] = 0;
+            named_bar_sync(1, kConsumerWarps * 32);
+        }
+
+        // epilogue: warp j transforms row j of the group
+        if (warp < rows) {
+            const int j = warp;
+            if (MODE == 0) {
+                float gv[4], uv[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    gv[q] = S.ep[j * 128 + lane * 4 + q];
+                    uv[q] = S.ep[(16 + j) * 128 + lane * 4 + q];
+                }
+                const size_t sv = (size_t)e * 2 * p.N + cb * 128 + lane * 4;
+                out_block4(gv, p.svh_a + sv, lane);
+                out_block4(uv, p.svh_a + sv + p.N, lane);
+                const uint2 su = *reinterpret_cast<const uint2*>(p.suh_d + (size_t)e * p.N + cb * 128 + lane * 4);
+                const __half2 s01 = u32_as_half2(su.x), s23 = u32_as_half2(su.y);
+                const float sd[4] = {__low2float(s01), __high2float(s01), __low2float(s23), __high2float(s23)};
+                float v[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(r16(act_gu(gv[q], uv[q], p.limit)), sd[q]);
+                had128_warp(v, lane);
+                uint2 o;
+                o.x = half2_as_u32(__floats2half2_rn(__fmul_rn(v[0], kHad), __fmul_rn(v[1], kHad)));
+                o.y = half2_as_u32(__floats2half2_rn(__fmul_rn(v[2], kHad), __fmul_rn(v[3], kHad)));
+                *reinterpret_cast<uint2*>(p.out + (size_t)(row0 + j) * p.N + cb * 128 + lane * 4) = o;
+            } else {
+#pragma unroll
+                for (int blk = 0; blk < 2; ++blk) {
+                    float y[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) y[q] = S.ep[j * 256 + blk * 128 + lane * 4 + q];
+                    const size_t c = (size_t)cb * 256 + blk * 128 + lane * 4;
+                    out_block4(y, p.svh_a + (size_t)e * p.N + c, lane);
+                    uint2 o;
+                    o.x = half2_as_u32(__floats2half2_rn(y[0], y[1]));
+                    o.y = half2_as_u32(__floats2half2_rn(y[2], y[3]));
+                    *reinterpret_cast<uint2*>(p.out + (size_t)(row0 + j) * p.N + c) = o;
+                }
+            }
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+    }
+}
+
+int gemv_units_bound(int groups_bound, int K, int N, int mode, int split)
+{
+    const int cols = mode == 0 ? 128 : 256;
+    return groups_bound * (N / cols) * split;
+}
+
+// buffer sizing over both passes (gate/up: I/128 column blocks, down: H/256)
+int gemv_units_alloc(int groups_bound, int H, int I, int split)
+{
+    const int cb = (I / 128 > H / 256) ? I / 128 : H / 256;
+    return groups_bound * cb * split;
+}
+
+cudaError_t launch_gemv(int mode, const GemvParams& p, int units_bound, cudaStream_t st)
+{
+    const size_t smem = sizeof(GemvSmem);
+    const void* fn = mode == 0 ? (const void*)exl3_gemv_kernel<0> : (const void*)exl3_gemv_kernel<1>;
+    cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err != cudaSuccess) return err;
+    int grid = 2 * num_sms();
+    if (units_bound < grid) grid = units_bound;
+    if (grid < 1) grid = 1;
+    if (mode == 0)
+        exl3_gemv_kernel<0><<<grid, kGemvThreads, smem, st>>>(p);
+    else
+        exl3_gemv_kernel<1><<<grid, kGemvThreads, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace dsv41

@@ -1,0 +1,85 @@
+// Internal launch interface shared by the kernel files and the C ABI (capi.cu).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace dsv41 {
+
+constexpr int kRowsPerGroup = 16;     // decode-GEMV row group (one mma M tile)
+constexpr int kPermSmallMax = 8192;   // routes handled by the single-CTA permutation
+constexpr int kPermSegment = 256;     // routes per warp segment in the multi-CTA permutation
+constexpr int kMaxExperts = 4096;
+
+// Routing permutation results (device pointers; int32 internally)
+struct PermBuffers {
+    int* counts;         // [E+1]
+    int* offsets;        // [E+1] exclusive
+    int* token_sorted;   // [N]
+    float* weight_sorted;// [N]
+    int* route_sorted;   // [N] flat route index of each sorted row
+    int* expert_sorted;  // [N] local expert of each sorted row (E for invalid)
+    int* route_pos;      // [N] sorted position of each flat route (-1 invalid)
+    int4* groups;        // [max_groups] {expert, row_begin, rows, 0} for GEMV experts
+    int* n_groups;       // [1]
+    int* fat_experts;    // [E] experts routed to the GEMM path
+    int* n_fat;          // [1]
+    int* seg_hist;       // [nseg][E+1] (multi-CTA path)
+    int64_t* counts64;   // optional [E+1] (reference contract, int64)
+    int64_t* offsets64;  // optional [E+1]
+};
+
+size_t perm_seg_hist_ints(int N, int E);
+bool perm_uses_small(int N, int E);
+int max_groups(int N, int E);
+
+cudaError_t launch_permute(const int64_t* ids, const float* weights, int N, int topk, int E,
+                           const int32_t* expert_map, int map_len, int fat_threshold,
+                           const PermBuffers& pb, cudaStream_t st);
+
+cudaError_t launch_prep(const void* x, int x_dtype, const int* token_sorted, const int* expert_sorted,
+                        const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
+                        cudaStream_t st);
+
+// Work lists for an explicit expert list over caller-permuted rows (run_batch semantics):
+// int32 counts/offsets copies, expert_sorted (-1 for rows of unlisted experts), GEMV groups of the
+// listed experts with <= fat rows (all when fat < 0) and the fat list; *nrows = total_rows.
+cudaError_t launch_list_setup(const int32_t* experts, int n_experts, const int64_t* counts64,
+                              const int64_t* offsets64, int E, int total_rows, int fat, const PermBuffers& pb,
+                              int* nrows, cudaStream_t st);
+
+struct GemvParams {
+    const int4* groups;
+    const int* n_groups;
+    const int64_t* tab_a;  // gate (gate/up pass) or down trellis addresses [E]
+    const int64_t* tab_b;  // up
+    const __half* xa;      // gate/up pass: xt_g [rows][K]; down pass: xt_d [rows][K]
+    const __half* xb;      // gate/up pass: xt_u
+    const __half* svh_a;   // gate/up pass: w13_svh [E][2][N]; down pass: w2_svh [E][N]
+    const __half* suh_d;   // gate/up pass: w2_suh [E][N]
+    __half* out;           // gate/up pass: xt_d [rows][N]; down pass: y [rows][N]
+    float* partials;       // split-K partials [units][4096]
+    int* counters;         // split-K arrival counters [units / split]
+    int* status;
+    int K, N, split;
+    float limit;
+};
+
+int gemv_units_bound(int groups_bound, int K, int N, int mode, int split);
+int gemv_units_alloc(int groups_bound, int H, int I, int split);
+size_t gemv_smem_bytes();
+cudaError_t launch_gemv(int mode, const GemvParams& p, int units_bound, cudaStream_t st);
+
+cudaError_t launch_combine(const __half* y, const int* route_pos, const float* w, int T, int topk,
+                           int H, int accumulate, float* out, cudaStream_t st);
+cudaError_t launch_scatter_add(const __half* y, const int* expert_list, int n_list,
+                               const int* counts, const int* offsets, const int* token_sorted,
+                               const float* weight_sorted, int H, int rows_bound, float* out,
+                               cudaStream_t st);
+
+cudaError_t launch_decode_dense(const void* trellis, int k, int n, __half* w, cudaStream_t st);
+
+int num_sms();
+
+}  // namespace dsv41

@@ -1,0 +1,218 @@
+// Row transforms and the weighted combine.
+//
+// prep:    xt = fp16(H128(fp16(x) * suh) * 2^-3.5) per 128-block, for gate and up of the row's
+//          expert (kernels/cpu_avx2/ft_core.h:96-102 prep_block; the fp16 cast of the hidden
+//          states is apply_exl3_fused_moe's x2d.half(), patches/vllm-exl3-host-dma.patch:224).
+// combine: out[t] = sum_j w[t, j] * y[route(t, j)] in fp32, routes in topk order
+//          (ft_core.h:686-696 / :929-930, the weighted accumulate; ct/ft_tier_cu_v.cu:103-127).
+// decode:  dense fp16 W from trellis, one warp per tile (ft_core.h:977-992 dense_weights).
+#include "common.cuh"
+#include "internal.h"
+
+#include <cuda_bf16.h>
+
+namespace dsv41 {
+
+__device__ __forceinline__ void load4_as_half(const void* x, int dtype, size_t idx, float (&v)[4])
+{
+    if (dtype == 0) {
+        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __half*>(x) + idx);
+        const __half2 a = u32_as_half2(u.x), b = u32_as_half2(u.y);
+        v[0] = __low2float(a); v[1] = __high2float(a); v[2] = __low2float(b); v[3] = __high2float(b);
+    } else if (dtype == 1) {
+        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(x) + idx);
+        v[0] = __uint_as_float(u.x << 16); v[1] = __uint_as_float(u.x & 0xffff0000u);
+        v[2] = __uint_as_float(u.y << 16); v[3] = __uint_as_float(u.y & 0xffff0000u);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] = r16(v[q]);
+    } else {
+        const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + idx);
+        v[0] = r16(f.x); v[1] = r16(f.y); v[2] = r16(f.z); v[3] = r16(f.w);
+    }
+}
+
+__device__ __forceinline__ void load4_half(const __half* p, float (&v)[4])
+{
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __half2 a = u32_as_half2(u.x), b = u32_as_half2(u.y);
+    v[0] = __low2float(a); v[1] = __high2float(a); v[2] = __low2float(b); v[3] = __high2float(b);
+}
+
+__device__ __forceinline__ void store4_half(__half* p, const float (&v)[4])
+{
+    uint2 u;
+    u.x = half2_as_u32(__floats2half2_rn(v[0], v[1]));
+    u.y = half2_as_u32(__floats2half2_rn(v[2], v[3]));
+    *reinterpret_cast<uint2*>(p) = u;
+}
+
+// one warp task = (sorted row p, 128-block b): both gate and up transforms of that block
+// rows p < *nrows; rows whose expert_sorted entry is negative are skipped
+__global__ void __launch_bounds__(256) prep_kernel(const void* x, int x_dtype, const int* token_sorted,
+                                                   const int* expert_sorted, const int* nrows,
+                                                   const __half* w13_suh, int H, __half* xt_g, __half* xt_u)
+{
+    const int lane = threadIdx.x & 31;
+    const int nvalid = *nrows;
+    const int nb = H / 128;
+    const long long tasks = (long long)nvalid * nb;
+    const long long wstride = (long long)gridDim.x * (blockDim.x >> 5);
+    for (long long tk = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tk < tasks; tk += wstride) {
+        const int p = (int)(tk / nb), b = (int)(tk % nb);
+        const int e = expert_sorted[p];
+        if (e < 0) continue;
+        const int t = token_sorted[p];
+        const int c = b * 128 + lane * 4;
+        float xv[4];
+        load4_as_half(x, x_dtype, (size_t)t * H + c, xv);
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+            float s[4], v[4];
+            load4_half(w13_suh + ((size_t)e * 2 + m) * H + c, s);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(xv[q], s[q]);
+            had128_warp(v, lane);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(v[q], kHad);
+            store4_half((m ? xt_u : xt_g) + (size_t)p * H + c, v);
+        }
+    }
+}
+
+cudaError_t launch_prep(const void* x, int x_dtype, const int* token_sorted, const int* expert_sorted,
+                        const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
+                        cudaStream_t st)
+{
+    const long long tasks = (long long)N * (H / 128);
+    long long blocks = (tasks + 7) / 8;
+    const long long cap = (long long)num_sms() * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    prep_kernel<<<(int)blocks, 256, 0, st>>>(x, x_dtype, token_sorted, expert_sorted, nrows, w13_suh, H, xt_g,
+                                             xt_u);
+    return cudaGetLastError();
+}
+
+// thread = (token t, 8 consecutive columns)
+__global__ void __launch_bounds__(256) combine_kernel(const __half* y, const int* route_pos, const float* w, int T,
+                                                      int topk, int H, int accumulate, float* out)
+{
+    const int chunks = H / 8;
+    const long long n = (long long)T * chunks;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / chunks), c = (int)(i % chunks) * 8;
+        float acc[8];
+        float* o = out + (size_t)t * H + c;
+        if (accumulate) {
+            const float4 a = *reinterpret_cast<const float4*>(o), b = *reinterpret_cast<const float4*>(o + 4);
+            acc[0] = a.x; acc[1] = a.y; acc[2] = a.z; acc[3] = a.w; acc[4] = b.x; acc[5] = b.y; acc[6] = b.z; acc[7] = b.w;
+        } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc[q] = 0.0f;
+        }
+        for (int j = 0; j < topk; ++j) {
+            const int pos = route_pos[t * topk + j];
+            if (pos < 0) continue;
+            const float wt = w[t * topk + j];
+            const uint4 u = *reinterpret_cast<const uint4*>(y + (size_t)pos * H + c);
+            const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const __half2 h = u32_as_half2(v[q]);
+                acc[2 * q] = __fmaf_rn(wt, __low2float(h), acc[2 * q]);
+                acc[2 * q + 1] = __fmaf_rn(wt, __high2float(h), acc[2 * q + 1]);
+            }
+        }
+        *reinterpret_cast<float4*>(o) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(o + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+}
+
+cudaError_t launch_combine(const __half* y, const int* route_pos, const float* w, int T, int topk, int H,
+                           int accumulate, float* out, cudaStream_t st)
+{
+    const long long n = (long long)T * (H / 8);
+    long long blocks = (n + 255) / 256;
+    const long long cap = (long long)num_sms() * 16;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    combine_kernel<<<(int)blocks, 256, 0, st>>>(y, route_pos, w, T, topk, H, accumulate, out);
+    return cudaGetLastError();
+}
+
+// Busy-expert rows accumulated into out with fp32 atomics (the reference fat path accumulates
+// into its out buffer the same way): for each listed expert, each of its rows adds w * y.
+__global__ void __launch_bounds__(256) scatter_add_kernel(const __half* y, const int* expert_list, int nl,
+                                                          const int* counts, const int* offsets,
+                                                          const int* token_sorted, const float* weight_sorted,
+                                                          int H, float* out)
+{
+    const int chunks = H / 8;
+    for (int li = blockIdx.y; li < nl; li += gridDim.y) {
+        const int e = expert_list[li];
+        const int c = counts[e], r0 = offsets[e];
+        const long long n = (long long)c * chunks;
+        for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+            const int r = r0 + (int)(i / chunks), col = (int)(i % chunks) * 8;
+            const float wt = weight_sorted[r];
+            const uint4 u = *reinterpret_cast<const uint4*>(y + (size_t)r * H + col);
+            const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+            float* o = out + (size_t)token_sorted[r] * H + col;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const __half2 h = u32_as_half2(v[q]);
+                atomicAdd(o + 2 * q, wt * __low2float(h));
+                atomicAdd(o + 2 * q + 1, wt * __high2float(h));
+            }
+        }
+    }
+}
+
+cudaError_t launch_scatter_add(const __half* y, const int* expert_list, int n_list, const int* counts,
+                               const int* offsets, const int* token_sorted, const float* weight_sorted, int H,
+                               int rows_bound, float* out, cudaStream_t st)
+{
+    dim3 grid(32, 64);
+    scatter_add_kernel<<<grid, 256, 0, st>>>(y, expert_list, n_list, counts, offsets, token_sorted, weight_sorted, H,
+                                              out);
+    return cudaGetLastError();
+}
+
+// one warp per 16x16 tile
+__global__ void __launch_bounds__(256) decode_dense_kernel(const uint32_t* trellis, int k, int n, __half* w)
+{
+    const int lane = threadIdx.x & 31;
+    const int tn_count = n / 16;
+    const long long tiles = (long long)(k / 16) * tn_count;
+    const LaneDecode ld = lane_decode_setup(lane);
+    const int r0 = (lane % 4) * 2, c0 = lane / 4;
+    for (long long tile = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tile < tiles;
+         tile += (long long)gridDim.x * (blockDim.x >> 5)) {
+        const uint32_t* tw = trellis + tile * kTileWords;
+        uint32_t b[4];
+        decode_lane(__ldg(tw + ld.w_hi), __ldg(tw + ld.w_lo), ld, b);
+        const int tk = (int)(tile / tn_count), tn = (int)(tile % tn_count);
+        __half* base = w + (size_t)(tk * 16) * n + tn * 16;
+        const int rows[4] = {r0, r0 + 8, r0, r0 + 8};
+        const int cols[4] = {c0, c0, c0 + 8, c0 + 8};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const __half2 h = u32_as_half2(b[q]);
+            base[(size_t)rows[q] * n + cols[q]] = __low2half(h);
+            base[(size_t)(rows[q] + 1) * n + cols[q]] = __high2half(h);
+        }
+    }
+}
+
+cudaError_t launch_decode_dense(const void* trellis, int k, int n, __half* w, cudaStream_t st)
+{
+    const long long tiles = (long long)(k / 16) * (n / 16);
+    long long blocks = (tiles + 7) / 8;
+    const long long cap = (long long)num_sms() * 16;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    decode_dense_kernel<<<(int)blocks, 256, 0, st>>>(static_cast<const uint32_t*>(trellis), k, n, w);
+    return cudaGetLastError();
+}
+
+}  // namespace dsv41

@@ -1,0 +1,140 @@
+/*
+ * dsv41_b200 -- C ABI of the B200 (sm_100a) routed-expert MoE FFN over EXL3 mul1 K=3 weights.
+ *
+ * Plain pointers and sizes only (no torch types). Every compute entry point is asynchronous on
+ * the caller's CUDA stream (`stream` is a cudaStream_t passed as void*; NULL = legacy default
+ * stream), allocates nothing, returns 0 on success or a negative DSV41_E* code, and leaves a
+ * message for dsv41_last_error(). Kernels never trap: a device-side wait that runs out writes a
+ * nonzero status word into the workspace, read back with dsv41_read_status().
+ *
+ * Reference interfaces replaced (paths inside the reference project 0xSero/dsv41-flash-offload):
+ *   dsv41_moe_forward       apply_exl3_fused_moe(x2d, ids, weights, layer, inners, expert_map,
+ *                           limit) -> out fp32 [T, H]: the routing prep
+ *                           (patches/vllm-exl3-host-dma.patch:203-312) plus the
+ *                           exllamav3_ext.exl3_moe launch contract (patch:315-449), and the
+ *                           busy-expert path apply_exl3_batched_fat (patch:182-201) for experts
+ *                           over fat_threshold rows; wrapped in the reference by
+ *                           ct/ct_vllm.py:181-225 (_fused)
+ *   dsv41_permute           the routing prep alone (patch:204-226, :300-312) and the split
+ *                           kernel's histogram/compaction (ct/ft_tier_cu_v.cu:16-101, ft_split)
+ *   dsv41_combine           the weighted accumulate of routed expert outputs into the fp32
+ *                           layer output (ct/ft_tier_cu_v.cu:103-127 ft_combine;
+ *                           kernels/cpu_avx2/ft_core.h:911-931)
+ *   dsv41_decode_dense      the reconstruct step of the fat path / LinearEXL3.get_weight_tensor
+ *                           (patch:182-201, pack/prepare_pack.py:64-65), restated from
+ *                           kernels/cpu_avx2/ft_core.h:977-992 (dense_weights)
+ *   dsv41_expert_gemm       runtime/dma_gemm.py:5-26 run_batch -> apply_exl3_batched_fat:
+ *                           busy experts' reconstruct + GEMM, accumulated into out
+ */
+#ifndef DSV41_B200_H
+#define DSV41_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSV41_ABI_VERSION 1
+
+enum {
+    DSV41_OK = 0,
+    DSV41_E_INVALID = -1,  /* bad argument / shape */
+    DSV41_E_CUDA = -2,     /* CUDA runtime error (launch or attribute) */
+    DSV41_E_WORKSPACE = -3 /* workspace too small */
+};
+
+enum { DSV41_DTYPE_F16 = 0, DSV41_DTYPE_BF16 = 1, DSV41_DTYPE_F32 = 2 };
+
+/* One MoE layer's expert weights, all device pointers (vllm_exl3 Exl3MoEMethod layout,
+ * patches/vllm-exl3-host-dma.patch:633-684 and its per-expert pointer tables, patch:66-69):
+ *   gate_ptrs/up_ptrs [E]  int64 addresses of int16 trellis [H/16][I/16][48]
+ *   down_ptrs [E]          int64 addresses of int16 trellis [I/16][H/16][48]
+ *   w13_suh [E][2][H], w13_svh [E][2][I], w2_suh [E][I], w2_svh [E][H]  fp16
+ * Every trellis address must be 16-byte aligned. H and I are multiples of 256. */
+typedef struct dsv41_moe_layer {
+    int32_t num_experts;
+    int32_t hidden;
+    int32_t intermediate;
+    int32_t reserved;
+    const int64_t* gate_ptrs;
+    const int64_t* up_ptrs;
+    const int64_t* down_ptrs;
+    const void* w13_suh;
+    const void* w13_svh;
+    const void* w2_suh;
+    const void* w2_svh;
+} dsv41_moe_layer;
+
+/* Options of one forward call.
+ *   fat_threshold: experts with more than this many rows use the tensor-core grouped GEMM
+ *                  (VLLM_EXL3_FAT_THRESHOLD, patch:146; 32 deployed); < 0 routes everything
+ *                  through the decode GEMV.
+ *   limit:         SwiGLU clamp (SWIGLU_LIMIT_DEFAULT 10.0, patch:5); 0 disables it.
+ *   expert_map:    optional device int32 [map_len] global -> local expert id (-1 = not local),
+ *                  as vLLM's expert_map; NULL = identity. */
+typedef struct dsv41_moe_options {
+    int32_t fat_threshold;
+    float limit;
+    const int32_t* expert_map;
+    int32_t map_len;
+    int32_t split_k; /* 0 = automatic */
+} dsv41_moe_options;
+
+/* Last error message of the calling thread ("" if none). */
+const char* dsv41_last_error(void);
+/* ABI version (DSV41_ABI_VERSION) and a build string. */
+int dsv41_abi_version(void);
+const char* dsv41_build_info(void);
+
+/* Workspace bytes that dsv41_moe_forward needs for T tokens x topk routes. */
+int dsv41_moe_workspace_size(int32_t T, int32_t topk, int32_t num_experts, int32_t hidden,
+                             int32_t intermediate, const dsv41_moe_options* opt, size_t* bytes);
+
+/* out[T][H] (fp32, overwritten) = sum over valid routes (t, j) of weights[t][j] * expert(x[t]).
+ *   x [T][H] of x_dtype (cast to fp16 first, as the reference does), ids [T][topk] int64
+ *   (negative or >= E = skipped), weights [T][topk] fp32. */
+int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
+                      const int64_t* ids, const float* weights, int32_t topk,
+                      const dsv41_moe_options* opt, float* out, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* Routing permutation (bit-exact, stable by (local expert, flat route index)):
+ *   counts/offsets [E+1] int64 (index E = invalid-route sentinel), token_sorted/route_sorted
+ *   [T*topk] int32, weight_sorted [T*topk] fp32, route_pos [T*topk] int32 (sorted position of
+ *   each flat route, -1 when skipped). Any output pointer may be NULL. */
+size_t dsv41_permute_workspace_size(int32_t T, int32_t topk, int32_t num_experts);
+int dsv41_permute(const int64_t* ids, const float* weights, int32_t T, int32_t topk,
+                  int32_t num_experts, const int32_t* expert_map, int32_t map_len,
+                  int64_t* counts, int64_t* offsets, int32_t* token_sorted, float* weight_sorted,
+                  int32_t* route_sorted, int32_t* route_pos, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* out[T][H] fp32 = sum_j weights[t][j] * y[route_pos[t*topk+j]][:] over route_pos >= 0;
+ * y [rows][H] fp16. accumulate != 0 adds into out instead of overwriting it. */
+int dsv41_combine(const void* y, const int32_t* route_pos, const float* weights, int32_t T,
+                  int32_t topk, int32_t hidden, int32_t accumulate, float* out, void* stream);
+
+/* Decode one trellis matrix [k/16][n/16][48] int16 into dense fp16 W [k][n] (bit-exact). */
+int dsv41_decode_dense(const void* trellis, int32_t k, int32_t n, void* w_out, void* stream);
+
+/* Busy-expert GEMM path on pre-permuted rows (run_batch semantics): for each listed expert e
+ * with counts[e] rows starting at offsets[e] of token_sorted/weight_sorted, out[token] +=
+ * weight * expert_e(x[token]). experts [n_experts] int32 (device). */
+int dsv41_expert_gemm(const dsv41_moe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
+                      const int32_t* experts, int32_t n_experts, const int64_t* counts,
+                      const int64_t* offsets, const int32_t* token_sorted,
+                      const float* weight_sorted, int32_t total_rows, float limit, float* out,
+                      void* workspace, size_t workspace_bytes, void* stream);
+int dsv41_expert_gemm_workspace_size(int32_t total_rows, int32_t n_experts, int32_t hidden,
+                                     int32_t intermediate, size_t* bytes);
+
+/* Synchronise `stream` and return the device status word of a workspace (0 = ok,
+ * 1 = a bounded device wait ran out), then clear it. */
+int dsv41_read_status(const void* workspace, void* stream, int32_t* status);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DSV41_B200_H */
