@@ -20,7 +20,10 @@ SYMBOLS = (
     "dsv41_last_error", "dsv41_abi_version", "dsv41_build_info", "dsv41_moe_workspace_size",
     "dsv41_moe_forward", "dsv41_permute_workspace_size", "dsv41_permute", "dsv41_combine",
     "dsv41_decode_dense", "dsv41_expert_gemm", "dsv41_expert_gemm_workspace_size", "dsv41_read_status",
+    "dsv41_set_stage_timing", "dsv41_read_stage_times",
 )
+N_STAGES = 7
+STAGE_NAMES = ("permute", "prep", "gemv_gateup", "gemm_gateup", "gemv_down", "gemm_down", "combine")
 
 
 class MoeLayer(C.Structure):
@@ -78,6 +81,10 @@ def load(path: str | None = None):
         L.dsv41_expert_gemm_workspace_size.argtypes = [i32, i32, i32, i32, C.POINTER(C.c_size_t)]
         L.dsv41_read_status.restype = C.c_int
         L.dsv41_read_status.argtypes = [vp, vp, C.POINTER(C.c_int32)]
+        L.dsv41_set_stage_timing.restype = C.c_int
+        L.dsv41_set_stage_timing.argtypes = [i32]
+        L.dsv41_read_stage_times.restype = C.c_int
+        L.dsv41_read_stage_times.argtypes = [C.POINTER(C.c_float), i32, C.POINTER(C.c_int32)]
         if L.dsv41_abi_version() != 1:
             raise Dsv41Error("libdsv41_b200.so ABI version mismatch")
         _lib = L

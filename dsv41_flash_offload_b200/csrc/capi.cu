@@ -151,6 +151,44 @@ static int check_layer(const dsv41_moe_layer* layer)
     return DSV41_OK;
 }
 
+// ------------------------------------------------------------------------------------------
+// optional stage timing (profiling): CUDA events at the forward's stage boundaries
+// ------------------------------------------------------------------------------------------
+struct StageTimer {
+    bool enabled = false;
+    int device = -1;
+    int calls = 0;      // recorded calls
+    bool active = false;  // current call records
+    cudaEvent_t ev[DSV41_TIMING_MAX_CALLS][DSV41_N_STAGES + 1];
+};
+static StageTimer g_timer;
+
+static void timer_begin(cudaStream_t st)
+{
+    g_timer.active = false;
+    if (!g_timer.enabled || g_timer.calls >= DSV41_TIMING_MAX_CALLS) return;
+    cudaStreamCaptureStatus cs;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev != g_timer.device) return;
+    g_timer.active = true;
+    cudaEventRecord(g_timer.ev[g_timer.calls][0], st);
+}
+
+static void timer_mark(cudaStream_t st, int boundary)
+{
+    if (g_timer.active) cudaEventRecord(g_timer.ev[g_timer.calls][boundary], st);
+}
+
+static void timer_end(cudaStream_t st)
+{
+    if (!g_timer.active) return;
+    cudaEventRecord(g_timer.ev[g_timer.calls][DSV41_N_STAGES], st);
+    g_timer.calls++;
+    g_timer.active = false;
+}
+
 // gate/up pass (GEMV groups, then GEMM for fat experts) and down pass over prepared rows
 static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuffers& pb, __half* xt_g, __half* xt_u,
                                      __half* xt_d, __half* y, float* partials, int* counters, int* status, int split,
@@ -195,7 +233,9 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
     gp.K = H;
     gp.N = I;
     if ((err = launch_gemv(0, gp, gemv_units_bound(groups_bound, H, I, 0, split), st)) != cudaSuccess) return err;
+    timer_mark(st, 3);
     if (fat >= 0 && (err = launch_gemm_gateup(ga, st)) != cudaSuccess) return err;
+    timer_mark(st, 4);
     gp.tab_a = layer->down_ptrs;
     gp.tab_b = nullptr;
     gp.xa = xt_d;
@@ -206,7 +246,9 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
     gp.K = I;
     gp.N = H;
     if ((err = launch_gemv(1, gp, gemv_units_bound(groups_bound, I, H, 1, split), st)) != cudaSuccess) return err;
+    timer_mark(st, 5);
     if (fat >= 0 && (err = launch_gemm_down(ga, st)) != cudaSuccess) return err;
+    timer_mark(st, 6);
     return cudaSuccess;
 }
 
@@ -262,9 +304,11 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     cudaError_t err;
     const PermBuffers pb = perm_buffers(workspace, L);
     int* status = at<int>(workspace, L.status);
+    timer_begin(st);
     if ((err = launch_permute(ids, weights, L.N, topk, E, o.expert_map, o.map_len, o.fat_threshold, pb, st)) !=
         cudaSuccess)
         return cuda_fail(err, "permute");
+    timer_mark(st, 1);
     __half* xt_g = at<__half>(workspace, L.xt_g);
     __half* xt_u = at<__half>(workspace, L.xt_u);
     __half* xt_d = at<__half>(workspace, L.xt_d);
@@ -272,12 +316,14 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     if ((err = launch_prep(x, x_dtype, pb.token_sorted, pb.expert_sorted, pb.offsets + E, L.N,
                            static_cast<const __half*>(layer->w13_suh), H, xt_g, xt_u, st)) != cudaSuccess)
         return cuda_fail(err, "prep");
+    timer_mark(st, 2);
     if ((err = run_expert_passes(layer, pb, xt_g, xt_u, xt_d, y, at<float>(workspace, L.partials),
                                  at<int>(workspace, L.counters), status, L.split, L.groups_bound, L.N, o.limit,
                                  o.fat_threshold, at<uint8_t>(workspace, L.gemm), st)) != cudaSuccess)
         return cuda_fail(err, "expert passes");
     if ((err = launch_combine(y, pb.route_pos, weights, T, topk, H, 0, out, st)) != cudaSuccess)
         return cuda_fail(err, "combine");
+    timer_end(st);
     return DSV41_OK;
 }
 
@@ -441,6 +487,53 @@ int dsv41_expert_gemm(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     if ((err = launch_scatter_add(y, experts, n_experts, pb.counts, pb.offsets, token_sorted, weight_sorted, H, total_rows,
                                   out, st)) != cudaSuccess)
         return cuda_fail(err, "scatter add");
+    return DSV41_OK;
+}
+
+int dsv41_set_stage_timing(int32_t enable)
+{
+    cudaError_t err;
+    int dev = 0;
+    if ((err = cudaGetDevice(&dev)) != cudaSuccess) return cuda_fail(err, "get device");
+    if (enable && !g_timer.enabled) {
+        if (g_timer.device >= 0 && g_timer.device != dev) {
+            // events belong to the device they were created on
+            int cur = dev;
+            cudaSetDevice(g_timer.device);
+            for (auto& row : g_timer.ev)
+                for (auto& e : row) cudaEventDestroy(e);
+            cudaSetDevice(cur);
+            g_timer.device = -1;
+        }
+        if (g_timer.device < 0) {
+            for (auto& row : g_timer.ev)
+                for (auto& e : row)
+                    if ((err = cudaEventCreate(&e)) != cudaSuccess) return cuda_fail(err, "event create");
+            g_timer.device = dev;
+        }
+    }
+    g_timer.enabled = enable != 0;
+    g_timer.calls = 0;
+    g_timer.active = false;
+    return DSV41_OK;
+}
+
+int dsv41_read_stage_times(float* ms, int32_t max_calls, int32_t* n_calls)
+{
+    if (!n_calls || (max_calls > 0 && !ms)) return fail(DSV41_E_INVALID, "NULL pointer");
+    const int n = g_timer.calls < max_calls ? g_timer.calls : max_calls;
+    cudaError_t err;
+    if (g_timer.calls > 0 && (err = cudaEventSynchronize(g_timer.ev[g_timer.calls - 1][DSV41_N_STAGES])) != cudaSuccess)
+        return cuda_fail(err, "event synchronize");
+    for (int c = 0; c < n; ++c)
+        for (int s = 0; s < DSV41_N_STAGES; ++s) {
+            float v = 0.0f;
+            if ((err = cudaEventElapsedTime(&v, g_timer.ev[c][s], g_timer.ev[c][s + 1])) != cudaSuccess)
+                return cuda_fail(err, "event elapsed");
+            ms[c * DSV41_N_STAGES + s] = v;
+        }
+    *n_calls = n;
+    g_timer.calls = 0;
     return DSV41_OK;
 }
 

@@ -39,6 +39,14 @@ def _env_int(name: str, default: int) -> int:
 # patch:146; 32 deployed by the reference's entrypoint). -1 keeps every expert on the GEMV.
 FAT_EXPERT_THRESHOLD = _env_int("VLLM_EXL3_FAT_THRESHOLD", -1)
 
+def _rows2d(t: torch.Tensor, T: int) -> torch.Tensor:
+    """[T, k] view of a routing tensor given as [T, k] or flat [T*k] (also for T == 0)."""
+    if t.dim() == 2 and t.shape[0] == T:
+        return t
+    k = t.shape[-1] if t.dim() >= 2 else (t.numel() // T if T else 0)
+    return t.reshape(T, k)
+
+
 _DTYPES = {torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
 
 
@@ -181,7 +189,7 @@ def apply_exl3_fused_moe(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Te
     if x2d.dtype not in _DTYPES:
         raise TypeError(f"unsupported activation dtype {x2d.dtype}")
     x2d = x2d.contiguous()
-    ids = ids.reshape(T, -1).to(device=dev, dtype=torch.int64).contiguous()
+    ids = _rows2d(ids, T).to(device=dev, dtype=torch.int64).contiguous()
     topk = ids.shape[1]
     weights = weights.reshape(T, topk).to(device=dev, dtype=torch.float32).contiguous()
     if out is None:
@@ -217,7 +225,7 @@ def apply_exl3_experts(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: to
     shape = x.shape
     x2d = x.reshape(-1, shape[-1])
     T = x2d.shape[0]
-    out = apply_exl3_fused_moe(x2d, topk_ids.reshape(T, -1), topk_weights.reshape(T, -1), layer, None, expert_map,
+    out = apply_exl3_fused_moe(x2d, _rows2d(topk_ids, T), _rows2d(topk_weights, T), layer, None, expert_map,
                                limit, **kw)
     return out.view(*shape[:-1], shape[-1])
 
@@ -249,7 +257,7 @@ def permute(ids: torch.Tensor, weights: torch.Tensor | None, num_experts: int, e
     L = _lib.load()
     dev = ids.device
     T = ids.shape[0]
-    ids = ids.reshape(T, -1).to(torch.int64).contiguous()
+    ids = _rows2d(ids, T).to(torch.int64).contiguous()
     k = ids.shape[1]
     N = T * k
     w = None if weights is None else weights.reshape(T, k).to(torch.float32).contiguous()

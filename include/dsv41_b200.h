@@ -134,6 +134,16 @@ int dsv41_expert_gemm_workspace_size(int32_t total_rows, int32_t n_experts, int3
  * 1 = a bounded device wait ran out), then clear it. */
 int dsv41_read_status(const void* workspace, void* stream, int32_t* status);
 
+/* Profiling (no counterpart in the reference; used by bench.py to time each kernel on the stream
+ * it runs on). While enabled, dsv41_moe_forward records CUDA events at its stage boundaries for up
+ * to DSV41_TIMING_MAX_CALLS calls (not under stream capture). dsv41_read_stage_times synchronises
+ * them and writes DSV41_N_STAGES times in ms per recorded call, in the order permute, row prep,
+ * gate/up GEMV, gate/up GEMM, down GEMV, down GEMM, combine; then it forgets them. */
+#define DSV41_N_STAGES 7
+#define DSV41_TIMING_MAX_CALLS 256
+int dsv41_set_stage_timing(int32_t enable);
+int dsv41_read_stage_times(float* ms, int32_t max_calls, int32_t* n_calls);
+
 #ifdef __cplusplus
 }
 #endif
