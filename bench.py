@@ -1,0 +1,450 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 routed-expert MoE layer (BASELINE.json metric:
+"MoE-layer tok/s (decode B=64, prefill 16k) @1/2/4/8 B200; % HBM/tensor peak").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one MoE-layer forward (E 384, H 4096, I 2048, top-8, EXL3 3.0-bpw trellis words, SwiGLU
+clamp 10) over one batch: the headline workload is BASELINE configs[1]'s decode batch of 64 tokens
+with uniform top-8 routing (all 384 experts HBM-resident). Synthetic seeded inputs stand in for real
+weights (no checkpoint): uniform random trellis words, +-1 suh, U(0.5,1.5)/64 svh, N(0,1) bf16
+hidden states, softmax(N(0,1)) top-8 routing. Layers and routing batches are cycled so every step
+streams ~2.7 GB of expert words (inputs far larger than the 126 MB L2).
+
+value   = tokens of all ranks / max-over-ranks device time of K steps (inputs resident in HBM)
+e2e     = the same through apply_exl3_fused_moe with pinned host inputs: H2D of x/ids/weights and
+          D2H of the fp32 output inside each timed step
+roofline= the dominant kernel (decode-GEMV gate/up pass): algorithmic bytes (distinct routed
+          experts' gate+up trellis and scales, activations in, down-input out) / its average
+          duration from CUDA events on its own stream inside the timed region, against the
+          measured HBM copy bandwidth (MEASURED_PEAKS.json)
+cpu_baseline / --impl reference = the reference's own AVX2 CPU expert tier
+          (kernels/cpu_avx2/ft_tier_ext.cpp tier_forward, built into oracle/_ref) on the same
+          decode batches, all host cores, rank 0 only.
+N > 1 runs independent replicas (weak scaling; the expert-parallel path is a separate workload).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+E, H, I, TOPK = 384, 4096, 2048, 8
+LIMIT = 10.0
+METRIC = "MoE-layer tok/s (decode B=64, prefill 16k) @1/2/4/8 B200; % HBM/tensor peak"
+TILE_BYTES_PER_MATRIX = (H // 16) * (I // 16) * 96          # 3,145,728
+EXPERT_BYTES = 3 * TILE_BYTES_PER_MATRIX + (2 * H + 2 * I + I + H) * 2   # 9,474,048
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--layers", type=int, default=4, help="layers cycled per step (defeats L2 reuse)")
+    ap.add_argument("--batches", type=int, default=8)
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------------------
+# environment helpers
+# ------------------------------------------------------------------------------------------
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), \
+            "MEASURED_PEAKS.json"
+    return 6650.0, 1590.0, 1400.0, "fallback (6.65 TB/s, 1.59 PFLOP/s)"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200", "-i", gpu_id], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                try:
+                    rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), power=float(parts[3]),
+                                     hw=parts[5], hwt=parts[6], swt=parts[7], swp=parts[8]))
+                except ValueError:
+                    pass
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        load = [r for r in rows if r["power"] > 250.0] or rows
+        reasons = sorted({name for r in load for name, key in (("hw_slowdown", "hw"), ("hw_thermal_slowdown", "hwt"),
+                                                               ("sw_thermal_slowdown", "swt"), ("sw_power_cap", "swp"))
+                          if r[key].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r["sm"] for r in load), "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": reasons, "samples": len(rows), "samples_under_load": len(load),
+                "power_w_max": max(r["power"] for r in rows)}
+
+
+# ------------------------------------------------------------------------------------------
+# workload
+# ------------------------------------------------------------------------------------------
+def make_batches(T, n, seed0, kind="uniform", zipf_s=1.1):
+    from dsv41_flash_offload_b200 import synth
+    out = []
+    for b in range(n):
+        x = synth.hidden_np(seed0 + b, T, H)
+        ids, w = synth.routing_np(seed0 + b, T, E, TOPK, kind=kind, zipf_s=zipf_s)
+        out.append((x, ids, w))
+    return out
+
+
+def to_device(batches, dev):
+    import torch
+    return [(torch.from_numpy(x).to(dev, torch.bfloat16), torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev))
+            for x, ids, w in batches]
+
+
+def launches_per_step(T, fat):
+    from dsv41_flash_offload_b200 import _lib  # noqa: F401
+    N = T * TOPK
+    perm = 1 if N <= 8192 else 3
+    return perm + 1 + 2 + 1 + (2 if fat >= 0 else 0)
+
+
+def time_steps(fn, K, W, dist_on):
+    """W untimed + K timed calls; device time by CUDA events on the current stream, max over ranks."""
+    import torch
+    for i in range(W):
+        fn(i)
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(K):
+        fn(W + i)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e)
+    if dist_on:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    return ms
+
+
+def stage_times(fn, K, W):
+    """Average per-stage device times (ms) over K calls recorded by the library's stage events."""
+    import ctypes as C
+    import torch
+    from dsv41_flash_offload_b200 import _lib
+    L = _lib.load()
+    for i in range(W):
+        fn(i)
+    torch.cuda.synchronize()
+    _lib.check(L.dsv41_set_stage_timing(1), "set_stage_timing")
+    K = min(K, 256)
+    for i in range(K):
+        fn(W + i)
+    buf = (C.c_float * (K * _lib.N_STAGES))()
+    n = C.c_int32()
+    _lib.check(L.dsv41_read_stage_times(buf, K, C.byref(n)), "read_stage_times")
+    _lib.check(L.dsv41_set_stage_timing(0), "set_stage_timing")
+    vals = list(buf)[: n.value * _lib.N_STAGES]
+    return {name: sum(vals[c * _lib.N_STAGES + s] for c in range(n.value)) / max(n.value, 1)
+            for s, name in enumerate(_lib.STAGE_NAMES)}
+
+
+def gateup_bytes(ids, T):
+    """Algorithmic bytes of one gate/up decode-GEMV launch: distinct experts' gate+up trellis, their
+    w13_svh and w2_suh channel scales, the transformed gate/up rows read once, the down-input rows
+    written once."""
+    import numpy as np
+    d = len(np.unique(ids))
+    rows = T * TOPK
+    return d * (2 * TILE_BYTES_PER_MATRIX + 2 * I * 2 + I * 2) + rows * 2 * H * 2 + rows * I * 2, d
+
+
+def layer_bytes(ids, T):
+    import numpy as np
+    d = len(np.unique(ids))
+    return d * EXPERT_BYTES + T * H * 2 + T * H * 4 + T * TOPK * 12
+
+
+def traffic_from_profile():
+    """dram bytes per launch of the gate/up GEMV from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", "gemv_gateup_decode_T64.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":")[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# ------------------------------------------------------------------------------------------
+# reference CPU tier (cpu_baseline and the --impl reference arm)
+# ------------------------------------------------------------------------------------------
+def reference_cpu_tier(layer, batches, seconds, T):
+    """tokens/s of the reference's AVX2 expert tier (tier_forward, mode -1 = its deployed auto mode)
+    over the decode batches, all host cores."""
+    import numpy as np
+    import torch
+    from oracle.oracle import load_ref_tier, ref_tier_path
+    path = ref_tier_path()
+    mod = load_ref_tier()
+    ncpu = os.cpu_count() or 1
+    pad = 2048  # int16 words: the AVX2 decoder reads up to 8 bytes past the last tile
+    w13 = torch.empty(layer.w13_trellis.numel() + pad, dtype=torch.int16)
+    w13[: layer.w13_trellis.numel()].copy_(layer.w13_trellis.reshape(-1))
+    w2 = torch.empty(layer.w2_trellis.numel() + pad, dtype=torch.int16)
+    w2[: layer.w2_trellis.numel()].copy_(layer.w2_trellis.reshape(-1))
+    g13 = layer.w13_trellis[0].numel()
+    g = layer.w13_trellis[0, 0].numel()
+    g2 = layer.w2_trellis[0].numel()
+    ptrs = torch.zeros(E, 3, dtype=torch.int64)
+    for e in range(E):
+        ptrs[e, 0] = w13.data_ptr() + 2 * (e * g13)
+        ptrs[e, 1] = w13.data_ptr() + 2 * (e * g13 + g)
+        ptrs[e, 2] = w2.data_ptr() + 2 * (e * g2)
+    mod.tier_init(ncpu, list(range(ncpu)), torch.zeros(16, dtype=torch.int64), torch.zeros(64 * H, dtype=torch.half),
+                  torch.zeros(64 * 24, dtype=torch.int32), torch.zeros(64 * H), -1, H, I, 1, 0)
+    mod.tier_set_limit(LIMIT)
+    cpu = lambda t: t.detach().cpu().contiguous()
+    mod.tier_add_layer(0, ptrs, cpu(layer.w13_suh[:, 0]), cpu(layer.w13_svh[:, 0]), cpu(layer.w13_suh[:, 1]),
+                       cpu(layer.w13_svh[:, 1]), cpu(layer.w2_suh), cpu(layer.w2_svh))
+    host = [(torch.from_numpy(x.astype(np.float16).astype(np.float32)), torch.from_numpy(ids.astype(np.int32)),
+             torch.from_numpy(w)) for x, ids, w in batches]
+    mod.tier_forward(0, *host[0], -1)  # warm-up (page-in)
+    calls, t0 = 0, time.perf_counter()
+    per = []
+    while True:
+        x, sel, w = host[calls % len(host)]
+        t1 = time.perf_counter()
+        mod.tier_forward(0, x, sel, w, -1)
+        per.append(time.perf_counter() - t1)
+        calls += 1
+        if time.perf_counter() - t0 >= seconds and calls >= 3:
+            break
+    total = time.perf_counter() - t0
+    mod.tier_stop()
+    return {"value": round(T * calls / total, 2), "unit": "tok/s", "cores": ncpu, "kind": "reference",
+            "sample": f"{calls} tier_forward calls (decode batches of {T} tokens x top-{TOPK}, mode -1 auto, "
+                      f"clamp {LIMIT}) in {total:.1f} s; median {statistics.median(per) * 1e3:.1f} ms/call; "
+                      f"{os.path.basename(os.path.dirname(path))} build of kernels/cpu_avx2/ft_tier_ext.cpp"}
+
+
+# ------------------------------------------------------------------------------------------
+def main():
+    a = parse()
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist_on = world > 1
+    if dist_on:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    T = a.tokens
+    hbm, tf_burst, tf_sus, peak_src = measured_peaks()
+
+    if a.impl == "reference":
+        if rank != 0:
+            if dist_on:
+                torch.distributed.destroy_process_group()
+            return
+        from dsv41_flash_offload_b200.exl3 import Exl3MoELayer
+        try:
+            layer = Exl3MoELayer.synthetic(E, H, I, seed=0, layer=0, device=dev)
+            batches = make_batches(T, a.batches, 1000)
+            cb = reference_cpu_tier(layer, batches, max(a.cpu_seconds, 5.0), T)
+        except FileNotFoundError as exc:
+            print(json.dumps({"impl": "reference", "unavailable": f"reference CPU tier not built: {exc}"}))
+            return
+        print(json.dumps({"metric": METRIC, "value": cb["value"], "unit": "tok/s", "n_gpus": a.gpus, "steps": a.steps,
+                          "warmup": a.warmup, "ms_per_step": round(1e3 * T / cb["value"], 4), "higher_is_better": True,
+                          "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+                          "data": "synthetic (seeded random EXL3 trellis words; N(0,1) hidden; softmax top-8 routing)",
+                          "config": {"workload": f"decode T={T}: one MoE layer E={E} H={H} I={I} top-{TOPK}, uniform "
+                                                 f"routing, reference AVX2 CPU tier on host cores"},
+                          "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                                      "d2h_bytes_per_step": 0}}))
+        if dist_on:
+            torch.distributed.destroy_process_group()
+        return
+
+    from dsv41_flash_offload_b200 import exl3
+    layers = [exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, layer=l, device=dev) for l in range(a.layers)]
+    host_batches = make_batches(T, a.batches, 1000 + 100 * rank)
+    batches = to_device(host_batches, dev)
+    out = torch.empty(T, H, dtype=torch.float32, device=dev)
+    fat = exl3.FAT_EXPERT_THRESHOLD
+
+    def step(i):
+        x, ids, w = batches[i % len(batches)]
+        exl3.apply_exl3_fused_moe(x, ids, w, layers[i % len(layers)], None, None, LIMIT, out=out)
+
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid).replace("GPU-", "")
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid or str(local))
+    ms = time_steps(step, a.steps, a.warmup, dist_on)
+    clocks = sampler.stop()
+    value = world * T * a.steps / (ms / 1e3)
+
+    # dominant kernel: per-stage events over the same steps
+    st = stage_times(step, a.steps, 2)
+    gb = [gateup_bytes(ids, T) for _, ids, _ in host_batches]
+    lb = [layer_bytes(ids, T) for _, ids, _ in host_batches]
+    bytes_gu = statistics.mean(b for b, _ in gb)
+    distinct = statistics.mean(d for _, d in gb)
+    achieved = bytes_gu / (st["gemv_gateup"] / 1e3) / 1e9
+    layer_gbs = statistics.mean(lb) / (ms / a.steps / 1e3) / 1e9
+    traffic = traffic_from_profile()
+
+    # end to end through the public API with pinned host buffers
+    hb = [(torch.from_numpy(x).to(torch.bfloat16).pin_memory(), torch.from_numpy(ids).pin_memory(),
+           torch.from_numpy(w).pin_memory()) for x, ids, w in host_batches]
+    dx, dids, dw = (torch.empty_like(t, device=dev) for t in hb[0])
+    out_host = torch.empty(T, H, dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        x, ids, w = hb[i % len(hb)]
+        dx.copy_(x, non_blocking=True)
+        dids.copy_(ids, non_blocking=True)
+        dw.copy_(w, non_blocking=True)
+        exl3.apply_exl3_fused_moe(dx, dids, dw, layers[i % len(layers)], None, None, LIMIT, out=out)
+        out_host.copy_(out, non_blocking=True)
+
+    e2e_ms = time_steps(e2e_step, a.steps, a.warmup, dist_on)
+    e2e_val = world * T * a.steps / (e2e_ms / 1e3)
+    h2d = hb[0][0].numel() * 2 + hb[0][1].numel() * 8 + hb[0][2].numel() * 4
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 (fp16 operands, fp32 accumulate; EXL3 3-bit weights decoded exactly)",
+        "data": "synthetic (seeded random EXL3 trellis words, +-1 suh, U(0.5,1.5)/64 svh; N(0,1) bf16 hidden; "
+                "softmax(N(0,1)) top-8 routing)",
+        "config": {"workload": f"decode T={T}: one MoE layer E={E} H={H} I={I} top-{TOPK} SwiGLU clamp {LIMIT}, "
+                               f"uniform routing, all experts HBM-resident (BASELINE configs[1])",
+                   "layers_cycled": a.layers, "routing_batches": a.batches,
+                   "l2": "inputs larger than L2: each step streams the distinct routed experts' words "
+                         f"(~{statistics.mean(lb) / 1e9:.2f} GB), layers and batches cycled",
+                   "parallelism": f"{world} independent replica(s)" if world > 1 else "single GPU",
+                   "fat_threshold": fat},
+        "roofline": {"bound": "hbm", "kernel": "exl3_gemv_kernel<0> (decode-GEMV gate/up + act + down-input)",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "traffic": traffic, "peak_source": f"{peak_src} hbm_gbs (copy bandwidth)",
+                     "bytes_per_launch": round(bytes_gu), "distinct_experts_per_step": round(distinct, 1),
+                     "avg_launch_ms": round(st["gemv_gateup"], 5)},
+        "layer_hbm": {"achieved_gbs": round(layer_gbs, 1), "frac": round(layer_gbs / hbm, 4),
+                      "bytes_per_step": round(statistics.mean(lb))},
+        "stage_ms": {k: round(v, 5) for k, v in st.items()},
+        "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": T * H * 4},
+        "gpu_launches": a.steps * launches_per_step(T, fat),
+        "clocks": clocks,
+    }
+
+    if not a.no_sweep:
+        sweep = {}
+        for Ts in (1, 8, 32, 64):
+            hbs = make_batches(Ts, 4, 2000 + Ts)
+            bs = to_device(hbs, dev)
+            o2 = torch.empty(Ts, H, dtype=torch.float32, device=dev)
+
+            def sstep(i, bs=bs, o2=o2):
+                x, ids, w = bs[i % len(bs)]
+                exl3.apply_exl3_fused_moe(x, ids, w, layers[i % len(layers)], None, None, LIMIT, out=o2)
+
+            n = 100
+            sms = time_steps(sstep, n, 5, dist_on)
+            sst = stage_times(sstep, 64, 2)
+            lbs = statistics.mean(layer_bytes(ids, Ts) for _, ids, _ in hbs)
+            gbs = statistics.mean(gateup_bytes(ids, Ts)[0] for _, ids, _ in hbs)
+            sweep[str(Ts)] = {"tok_s": round(world * Ts * n / (sms / 1e3), 1), "ms_per_step": round(sms / n, 5),
+                              "layer_hbm_frac": round(lbs / (sms / n / 1e3) / 1e9 / hbm, 4),
+                              "gemv_gateup_hbm_frac": round(gbs / (sst["gemv_gateup"] / 1e3) / 1e9 / hbm, 4)}
+        line["sweep"] = sweep
+
+    if not a.no_prefill:
+        Tp = 16384
+        hp = make_batches(Tp, 1, 3000, kind="zipf", zipf_s=1.1)
+        bp = to_device(hp, dev)
+        op = torch.empty(Tp, H, dtype=torch.float32, device=dev)
+
+        def pstep(i):
+            x, ids, w = bp[0]
+            exl3.apply_exl3_fused_moe(x, ids, w, layers[i % len(layers)], None, None, LIMIT, out=op)
+
+        n = 6
+        pms = time_steps(pstep, n, 2, dist_on)
+        pst = stage_times(pstep, 3, 1)
+        flops = 2.0 * Tp * TOPK * 3 * H * I
+        import numpy as np
+        cnt = np.bincount(hp[0][1].reshape(-1), minlength=E)
+        line["prefill"] = {"workload": f"prefill T={Tp}, Zipf(1.1) top-{TOPK}", "tok_s": round(world * Tp * n / (pms / 1e3), 1),
+                           "ms_per_step": round(pms / n, 3), "tensor_tflops": round(flops / (pms / n / 1e3) / 1e12, 1),
+                           "tensor_frac_of_bf16_peak": round(flops / (pms / n / 1e3) / 1e12 / tf_burst, 4),
+                           "experts_over_32_rows": int((cnt > 32).sum()), "max_rows": int(cnt.max()),
+                           "path": "decode-GEMV row groups" if fat < 0 else f"GEMM for experts > {fat} rows",
+                           "stage_ms": {k: round(v, 3) for k, v in pst.items()}}
+
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        try:
+            line["cpu_baseline"] = reference_cpu_tier(layers[0], host_batches, a.cpu_seconds, T)
+        except FileNotFoundError as exc:
+            line["cpu_baseline"] = {"value": None, "unavailable": str(exc)}
+
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
