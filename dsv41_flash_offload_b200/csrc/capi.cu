@@ -223,6 +223,7 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
     gp.status = status;
     gp.split = split;
     gp.limit = limit;
+    gp.k16 = 65536u;
     gp.tab_a = layer->gate_ptrs;
     gp.tab_b = layer->up_ptrs;
     gp.xa = xt_g;

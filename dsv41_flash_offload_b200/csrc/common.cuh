@@ -80,6 +80,56 @@ __device__ __forceinline__ void decode_lane(uint32_t whi, uint32_t wlo, const La
 }
 
 // ------------------------------------------------------------------------------------------
+// Pipe-balanced decode (used by the GEMV kernels). Lane t's 8 states all lie in the 64 stream bits
+// that start at stream byte 3t-4 (mod 96): with that window in (hi, lo), state j is bits
+// [29-3j, 45-3j) for every lane, so all shifts are immediates. The window is assembled from three
+// words with two funnel shifts by 8*(byte offset % 4).
+//
+// Measured on B200 (sm_100a, one SM, independent chains): IMAD, DP4A and HFMA2 share one pipe at
+// half rate (16 lanes/clk per SM sub-partition); SHF, LOP3 and PRMT share another at half rate;
+// the two co-issue; mul.hi and bfe run at quarter rate. Per lane and tile the decode below issues
+// IMAD x8 + DP4A x8 + HFMA2 x4 + IMAD x1 (one half2 pack) on the first pipe and funnel/shift x9 +
+// LOP3 x7 + PRMT x4 (state 7 is byte aligned: one PRMT extracts it; three half2 packs) on the
+// second, about 21 each. `k16` must be the run-time value 65536 so the pack stays an IMAD.
+// ------------------------------------------------------------------------------------------
+struct LaneWindow {
+    int q0, q1, q2;  // word indices of the window
+    uint32_t r8;     // left funnel shift (0, 8, 16, 24)
+};
+
+__device__ __forceinline__ LaneWindow lane_window_setup(int t)
+{
+    const int b0 = (3 * t - 4 + 96) % 96;
+    LaneWindow w;
+    w.q0 = b0 >> 2;
+    w.q1 = (w.q0 + 1) % kTileWords;
+    w.q2 = (w.q0 + 2) % kTileWords;
+    w.r8 = 8u * (uint32_t)(b0 & 3);
+    return w;
+}
+
+__device__ __forceinline__ void decode_lane_u(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t r8, uint32_t k16,
+                                              uint32_t (&b)[4])
+{
+    const uint32_t hi = __funnelshift_l(w1, w0, r8);
+    const uint32_t lo = __funnelshift_l(w2, w1, r8);
+    uint32_t s[8];
+#pragma unroll
+    for (int j = 0; j < 5; ++j) s[j] = __funnelshift_r(lo, hi, 29 - 3 * j) & 0xffffu;
+    s[5] = (lo >> 14) & 0xffffu;
+    s[6] = (lo >> 11) & 0xffffu;
+    s[7] = __byte_perm(lo, 0u, 0x4421);  // bits [8, 24): bytes 1, 2 of lo, zero above
+    const __half2 kinv = u32_as_half2((uint32_t)kKinvBits * 0x10001u);
+    const __half2 kbias = u32_as_half2((uint32_t)kKbiasBits * 0x10001u);
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+        const uint32_t c0 = state_code(s[j]), c1 = state_code(s[j + 1]);
+        const uint32_t c = (j == 0) ? c1 * k16 + c0 : __byte_perm(c0, c1, 0x5410);
+        b[j >> 1] = half2_as_u32(__hfma2(u32_as_half2(c), kinv, kbias));
+    }
+}
+
+// ------------------------------------------------------------------------------------------
 // fp16 rounding helper and the 128-point Walsh-Hadamard transform over a warp
 // (lane holds elements lane*4 + q, q = 0..3; stage order w = 1, 2, 4, ..., 64 as the reference's
 // had128, ft_core.h:89-94, so every fp32 intermediate is the same)

@@ -135,7 +135,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) exl3_gemv_kernel(const GemvPa
     }
 
     // ------------------------------ consumer warps ------------------------------
-    const LaneDecode ld = lane_decode_setup(lane);
+    const LaneWindow lw = lane_window_setup(lane);
+    const uint32_t k16 = p.k16;
     const int mat = MODE == 0 ? (warp >> 3) : 0;
     const int tile_in_row = warp;  // byte offset warp * 96 inside a staged 1536-byte k-row
     const uint32_t x_lane = ((lane & 7) + ((lane >> 3) & 1) * 8) * kXRowStride + ((lane >> 4) & 1) * 16;
@@ -155,7 +156,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) exl3_gemv_kernel(const GemvPa
             for (int r = 0; r < kStageRows; ++r) {
                 const uint32_t* tw = trow + r * (kRowBytes / 4);
                 uint32_t b[4];
-                decode_lane(tw[ld.w_hi], tw[ld.w_lo], ld, b);
+                decode_lane_u(tw[lw.q0], tw[lw.q1], tw[lw.q2], lw.r8, k16, b);
                 uint32_t a[4];
                 ldmatrix_x4(a, xaddr + r * 32);
                 mma_16816(acc0, a, b[0], b[1]);

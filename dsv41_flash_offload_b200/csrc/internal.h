@@ -64,6 +64,7 @@ struct GemvParams {
     int* status;
     int K, N, split;
     float limit;
+    uint32_t k16;          // 65536, passed at run time (keeps the decode multiplies on the FMA pipe)
 };
 
 int gemv_units_bound(int groups_bound, int K, int N, int mode, int split);

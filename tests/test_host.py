@@ -63,6 +63,33 @@ def test_register_decode_restatement_matches_oracle(oracle):
                 assert _funnel_r(lo, hi, base - 3 * j) & 0xFFFF == ref[8 * t + j]
 
 
+def _funnel_l(lo, hi, s):
+    return (((hi << 32 | lo) << (s & 31)) >> 32) & 0xFFFFFFFF
+
+
+def test_uniform_window_decode_restatement_matches_oracle(oracle):
+    """decode_lane_u() (csrc/common.cuh): lane t's 64-bit window = 8 stream bytes from byte 3t-4,
+    assembled from 3 words with two left funnel shifts by 8*(b0%4); state j = bits [29-3j, 45-3j):
+    states 0-4 straddle (hi, lo) and come from a right funnel shift, 5-7 lie in lo (state 7 is
+    bytes 1-2 of lo, which one byte permute extracts)."""
+    rng = np.random.default_rng(2)
+    for _ in range(40):
+        tile = rng.integers(0, 65536, 48, dtype=np.uint16)
+        words = [int(tile[2 * i]) | int(tile[2 * i + 1]) << 16 for i in range(24)]
+        ref = oracle.states(tile)
+        for t in range(32):
+            b0 = (3 * t - 4) % 96
+            q, r8 = b0 // 4, 8 * (b0 % 4)
+            w0, w1, w2 = words[q], words[(q + 1) % 24], words[(q + 2) % 24]
+            hi = _funnel_l(w1, w0, r8)
+            lo = _funnel_l(w2, w1, r8)
+            for j in range(5):
+                assert _funnel_r(lo, hi, 29 - 3 * j) & 0xFFFF == ref[8 * t + j]
+            for j in range(5, 7):
+                assert (lo >> (29 - 3 * j)) & 0xFFFF == ref[8 * t + j]
+            assert ((lo >> 8) & 0xFF) | (((lo >> 16) & 0xFF) << 8) == ref[8 * t + 7]
+
+
 def test_half_fma_decode_matches_oracle_for_all_states(oracle):
     """(0x6400 | bytesum) as fp16 = 1024 + s exactly; one fp16 rounding of (1024+s)*KINV + KBIAS
     (what HFMA2 computes) equals the oracle's decoded weight for all 65536 states."""
