@@ -139,7 +139,8 @@ def launches_per_step(T, fat):
     from dsv41_flash_offload_b200 import _lib  # noqa: F401
     N = T * TOPK
     perm = 1 if N <= 8192 else 3
-    return perm + 1 + 2 + 1 + (2 if fat >= 0 else 0)
+    # permute, prep, 2 decode-GEMV passes, combine (+ GEMM plan and 2 tcgen05 GEMM passes)
+    return perm + 1 + 2 + 1 + (3 if fat >= 0 else 0)
 
 
 def time_steps(fn, K, W, dist_on):
@@ -422,15 +423,25 @@ def main():
 
         n = 6
         pms = time_steps(pstep, n, 2, dist_on)
-        pst = stage_times(pstep, 3, 1)
+        pst = stage_times(pstep, 4, 1)
         flops = 2.0 * Tp * TOPK * 3 * H * I
         import numpy as np
         cnt = np.bincount(hp[0][1].reshape(-1), minlength=E)
-        line["prefill"] = {"workload": f"prefill T={Tp}, Zipf(1.1) top-{TOPK}", "tok_s": round(world * Tp * n / (pms / 1e3), 1),
-                           "ms_per_step": round(pms / n, 3), "tensor_tflops": round(flops / (pms / n / 1e3) / 1e12, 1),
-                           "tensor_frac_of_bf16_peak": round(flops / (pms / n / 1e3) / 1e12 / tf_burst, 4),
-                           "experts_over_32_rows": int((cnt > 32).sum()), "max_rows": int(cnt.max()),
-                           "path": "decode-GEMV row groups" if fat < 0 else f"GEMM for experts > {fat} rows",
+        busy_rows = int(cnt[cnt > fat].sum()) if fat >= 0 else 0
+        gemm_ms = pst["gemm_gateup"] + pst["gemm_down"]
+        gemm_tf = 2.0 * busy_rows * 3 * H * I / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 and busy_rows else 0.0
+        line["prefill"] = {"workload": f"prefill T={Tp}, Zipf(1.1) top-{TOPK} (BASELINE configs[2])",
+                           "tok_s": round(world * Tp * n / (pms / 1e3), 1), "ms_per_step": round(pms / n, 3),
+                           "layer_tflops": round(flops / (pms / n / 1e3) / 1e12, 1),
+                           "layer_frac_of_bf16_peak": round(flops / (pms / n / 1e3) / 1e12 / tf_burst, 4),
+                           "experts_over_32_rows": int((cnt > 32).sum()), "busy_rows": busy_rows,
+                           "max_rows": int(cnt.max()),
+                           "path": "decode-GEMV row groups" if fat < 0 else
+                                   f"tcgen05 GEMM for experts > {fat} rows, decode-GEMV for the rest",
+                           "roofline": {"bound": "tensor", "kernel": "exl3_gemm_kernel<0>+<1> (decode-to-smem tcgen05)",
+                                        "achieved": round(gemm_tf, 1), "peak": tf_burst, "unit": "TFLOP/s",
+                                        "frac": round(gemm_tf / tf_burst, 4), "peak_sustained": tf_sus,
+                                        "peak_source": f"{peak_src} bf16_tflops (cuBLAS bf16 GEMM, burst)"},
                            "stage_ms": {k: round(v, 3) for k, v in pst.items()}}
 
     if rank == 0 and world == 1 and not a.no_cpu_baseline:

@@ -136,7 +136,9 @@ static PermBuffers perm_buffers(void* ws, const Layout& L)
     return pb;
 }
 
-constexpr int kExpertGemmFat = -1;  // busy experts use the GEMV groups until the tcgen05 GEMM is enabled
+// run_batch semantics: listed experts with more rows than this use the tcgen05 GEMM, the rest the
+// decode GEMV (the reference's FAT_EXPERT_THRESHOLD as deployed, docker/entrypoint.sh:69)
+constexpr int kExpertGemmFat = 32;
 
 static int check_layer(const dsv41_moe_layer* layer)
 {

@@ -1,13 +1,576 @@
-// Busy-expert GEMM path (see gemm.h).
+// Busy-expert ("fat") path: decode-to-shared-memory + tcgen05/TMEM grouped GEMM.
+//
+// Replaces apply_exl3_batched_fat (patches/vllm-exl3-host-dma.patch:182-201: reconstruct fp16 W,
+// then a 128x128 FP16 GEMM per busy expert; runtime/dma_gemm.py:5-26) with one persistent kernel
+// per pass in which the weights are decoded straight into the tensor-core operand layout:
+//   pass 0 (gate/up): D_g, D_u [rows x 128 features] = xt_{g,u} . W_{g,u}; epilogue per row:
+//                     out_block, SwiGLU clamp, fp16, down-input transform -> xt_d
+//   pass 1 (down):    D [rows x 128 features] = xt_d . W_d; epilogue: out_block -> y (fp16)
+// Work unit = (busy expert, row pass of 256 (gate/up) or 512 (down) rows, 128-feature block).
+// One CTA per SM, 10 warps:
+//   warp 0     producer: TMA (cp.async.bulk.tensor, SWIZZLE_128B, no multicast) of 128-row x 64-k
+//              activation tiles and 1-D bulk copies of the trellis k-rows, 2-stage mbarrier ring
+//   warp 1     TMEM allocator (512 columns) and single-thread tcgen05.mma issuer
+//              (kind::f16, M=128, N=128, K=16, fp32 accumulators in TMEM); tcgen05.commit frees
+//              a stage and signals the finished accumulators
+//   warps 2-9  decoders: each lane decodes its 8 weights of a 16x16 tile in registers (the same
+//              exact decode as the GEMV) and stores them as K-major 128B-swizzled fp16 B-operand
+//              rows; after the last k chunk they are the epilogue (tcgen05.ld, one row per thread,
+//              128-point Hadamard in registers)
+// Experts with more rows than one pass reuse each decoded weight for 256/512 rows.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "gemm.h"
 #include "internal.h"
 
 namespace dsv41 {
 
-size_t gemm_scratch_bytes(int N, int E, int H, int I) { return 256; }
+constexpr int kGemmThreads = 320;
+constexpr int kBM = 128;        // rows per M tile (TMEM lanes)
+constexpr int kBN = 128;        // features per unit (TMEM columns per accumulator)
+constexpr int kBK = 64;         // k per chunk (one 128-byte swizzle row of fp16)
+constexpr int kGStages = 2;
+constexpr int kTileA = kBM * kBK * 2;   // 16 KB
+constexpr int kTileB = kBN * kBK * 2;   // 16 KB
+constexpr int kTrRow = 8 * kTileBytes;  // 768 B: 8 n-tiles of one k-tile row
 
-cudaError_t launch_gemm_gateup(const GemmArgs& a, cudaStream_t st) { return cudaErrorNotSupported; }
-cudaError_t launch_gemm_down(const GemmArgs& a, cudaStream_t st) { return cudaErrorNotSupported; }
+template <int MODE>
+struct GemmCfg {
+    static constexpr int nmat = MODE == 0 ? 2 : 1;
+    static constexpr int mtiles = MODE == 0 ? 2 : 4;      // M tiles per pass
+    static constexpr int rows_per_pass = mtiles * kBM;
+    static constexpr int a_bytes = nmat * mtiles * kTileA;
+    static constexpr int b_bytes = nmat * kTileB;
+    static constexpr int t_bytes = nmat * 4 * kTrRow;
+    static constexpr int stage_bytes = a_bytes + b_bytes + t_bytes;   // multiple of 1024
+    static constexpr int smem_bytes = kGStages * stage_bytes + 1024 /* align */ + 256 /* barriers */;
+};
+
+struct GemmParams {
+    CUtensorMap tm_a;       // xt_g (gate/up) or xt_d (down): [rows][K] fp16
+    CUtensorMap tm_b;       // xt_u (gate/up)
+    const int4* passes;     // {expert, row_begin, rows, 0}
+    const int* n_passes;
+    const int64_t* tab_a;   // gate / down trellis addresses
+    const int64_t* tab_b;   // up
+    const __half* svh_a;    // gate/up: w13_svh [E][2][N]; down: w2_svh [E][N]
+    const __half* suh_d;    // gate/up: w2_suh [E][N]
+    __half* out;            // gate/up: xt_d [rows][N]; down: y [rows][N]
+    int* status;
+    int K, N;
+    float limit;
+    uint32_t k16;
+};
+
+// ---------------------------------------------------------------------------------------------
+// tcgen05 / TMA primitives
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
+{
+    // K-major, SWIZZLE_128B canonical layout: 8-row atoms of 128 B rows, atoms 1024 B apart
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16, fp16 A/B, fp32 D, K-major A and B, N = 128, M = 128
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
+{
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+        "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+        "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int c0, int c1, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// 128-point Hadamard of one row held by one thread, stage order w = 1..64 (ft_core.h:89-94)
+__device__ __forceinline__ void had128_thread(float (&v)[128])
+{
+#pragma unroll
+    for (int w = 1; w < 128; w <<= 1)
+#pragma unroll
+        for (int b = 0; b < 128; b += 2 * w)
+#pragma unroll
+            for (int i = b; i < b + w; ++i) {
+                const float p = v[i], q = v[i + w];
+                v[i] = p + q;
+                v[i + w] = p - q;
+            }
+}
+
+__device__ __forceinline__ void load_half8(const __half* p, float* dst)
+{
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const __half2 h = u32_as_half2(w[q]);
+        dst[2 * q] = __low2float(h);
+        dst[2 * q + 1] = __high2float(h);
+    }
+}
+
+// y = r16(H128(r16(y)) * HAD * svh), svh = 128 fp16 scales
+__device__ __forceinline__ void out_block128(float (&v)[128], const __half* svh)
+{
+#pragma unroll
+    for (int i = 0; i < 128; ++i) v[i] = r16(v[i]);
+    had128_thread(v);
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        float s[8];
+        load_half8(svh + c * 8, s);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[c * 8 + q] = r16(__fmul_rn(__fmul_rn(v[c * 8 + q], kHad), s[q]));
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// kernel
+// ---------------------------------------------------------------------------------------------
+template <int MODE>
+__global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid_constant__ GemmParams p)
+{
+    using Cfg = GemmCfg<MODE>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_addr(smem_raw);
+    uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGStages * Cfg::stage_bytes);
+    uint64_t* a_full = bars;                 // [kGStages]
+    uint64_t* t_full = bars + kGStages;      // [kGStages]
+    uint64_t* b_full = bars + 2 * kGStages;  // [kGStages]
+    uint64_t* mma_done = bars + 3 * kGStages;
+    uint64_t* acc_full = bars + 4 * kGStages;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 4 * kGStages + 1);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * kGStages + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_fb = p.N / kBN;
+    const int n_chunks = p.K / kBK;
+    const int n_units = (*p.n_passes) * n_fb;
+    const int ntile_row = p.N / 16;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kGStages; ++s) {
+            mbar_init(&a_full[s], 1);
+            mbar_init(&t_full[s], 1);
+            mbar_init(&b_full[s], 8);
+            mbar_init(&mma_done[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_addr(tmem_slot))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    auto stage_a = [&](int s, int mat, int mt) { return smem + s * Cfg::stage_bytes + (mat * Cfg::mtiles + mt) * kTileA; };
+    auto stage_b = [&](int s, int mat) { return smem + s * Cfg::stage_bytes + Cfg::a_bytes + mat * kTileB; };
+    auto stage_t = [&](int s, int mat, int kt) {
+        return smem + s * Cfg::stage_bytes + Cfg::a_bytes + Cfg::b_bytes + (mat * 4 + kt) * kTrRow;
+    };
+
+    if (warp == 0) {
+        // ---------------------------------- producer ----------------------------------
+        uint32_t it = 0;
+        bool ok = true;
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_a)) : "memory");
+            if (MODE == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_b)) : "memory");
+        }
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            const int pass = u / n_fb, fb = u % n_fb;
+            const int4 P = p.passes[pass];
+            const int e = P.x, row0 = P.y, rows = P.z;
+            const int act_mt = (rows + kBM - 1) / kBM;
+            const uint8_t* tr[2] = {reinterpret_cast<const uint8_t*>(p.tab_a[e]),
+                                    MODE == 0 ? reinterpret_cast<const uint8_t*>(p.tab_b[e]) : nullptr};
+            for (int c = 0; c < n_chunks; ++c, ++it) {
+                const int s = it % kGStages;
+                const uint32_t round = it / kGStages;
+                if (!mbar_wait_bounded(&mma_done[s], (round & 1) ^ 1, abort_flag, p.status)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&a_full[s], Cfg::nmat * act_mt * kTileA);
+                    for (int mat = 0; mat < Cfg::nmat; ++mat)
+                        for (int mt = 0; mt < act_mt; ++mt)
+                            tma_load_2d(stage_a(s, mat, mt), mat ? &p.tm_b : &p.tm_a, c * kBK, row0 + mt * kBM, &a_full[s]);
+                    mbar_arrive_expect_tx(&t_full[s], Cfg::t_bytes);
+                }
+                __syncwarp();
+                if (lane < Cfg::nmat * 4) {
+                    const int mat = lane / 4, kt = lane % 4;
+                    const uint8_t* src = tr[mat] + ((size_t)(c * 4 + kt) * ntile_row + fb * 8) * kTileBytes;
+                    bulk_g2s(stage_t(s, mat, kt), src, kTrRow, &t_full[s], l2_policy_evict_first());
+                }
+            }
+        }
+        if (!ok && lane == 0) {
+            const uint32_t n_back = it < (uint32_t)kGStages ? it : (uint32_t)kGStages;
+            for (uint32_t q = 1; q <= n_back; ++q) {
+                const uint32_t j = it - q;
+                const uint64_t t0 = globaltimer_ns();
+                while (!(mbar_try_wait(&a_full[j % kGStages], (j / kGStages) & 1) &&
+                         mbar_try_wait(&t_full[j % kGStages], (j / kGStages) & 1)) &&
+                       globaltimer_ns() - t0 < kWaitLimitNs) {}
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------- MMA issuer ----------------------------------
+        if (lane == 0) {
+            uint32_t it = 0, units_done = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++units_done) {
+                const int pass = u / n_fb;
+                const int rows = p.passes[pass].z;
+                const int act_mt = (rows + kBM - 1) / kBM;
+                for (int c = 0; c < n_chunks; ++c, ++it) {
+                    const int s = it % kGStages;
+                    const uint32_t round = it / kGStages;
+                    if (!mbar_wait_bounded(&a_full[s], round & 1, abort_flag, p.status) ||
+                        !mbar_wait_bounded(&b_full[s], round & 1, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    for (int mt = 0; mt < act_mt; ++mt)
+                        for (int mat = 0; mat < Cfg::nmat; ++mat) {
+                            const uint32_t d = tmem + (uint32_t)((mt * Cfg::nmat + mat) * kBN);
+                            const uint32_t a0 = smem_addr(stage_a(s, mat, mt)), b0 = smem_addr(stage_b(s, mat));
+#pragma unroll
+                            for (int kk = 0; kk < kBK / 16; ++kk)
+                                umma_f16(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), (c > 0 || kk > 0) ? 1u : 0u);
+                        }
+                    umma_commit(&mma_done[s]);
+                }
+                if (ok) umma_commit(acc_full);
+            }
+            // wait for the last MMAs before TMEM is released
+            if (it > 0) {
+                const uint32_t j = it - 1;
+                const uint64_t t0 = globaltimer_ns();
+                while (!mbar_try_wait(&mma_done[j % kGStages], (j / kGStages) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {}
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------- decoders + epilogue -------------------------------
+        const int d = warp - 2;                       // 0..7
+        const LaneWindow lw = lane_window_setup(lane);
+        const uint32_t k16 = p.k16;
+        const int r0 = (lane & 3) * 2, c0 = lane >> 2;
+        // decode assignment: gate/up: warp d -> matrix d/4, k-tile d%4, n-tiles 0..7
+        //                    down:    warp d -> k-tile d/2, n-tiles 4*(d%2) .. +3
+        const int dmat = MODE == 0 ? d / 4 : 0;
+        const int dkt = MODE == 0 ? d % 4 : d / 2;
+        const int nt0 = MODE == 0 ? 0 : 4 * (d % 2);
+        const int ntn = MODE == 0 ? 8 : 4;
+        const int quarter = warp & 3;                 // TMEM lanes this warp may access
+        uint32_t it = 0, units_done = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++units_done) {
+            const int pass = u / n_fb, fb = u % n_fb;
+            const int4 P = p.passes[pass];
+            const int e = P.x, row0 = P.y, rows = P.z;
+            for (int c = 0; c < n_chunks; ++c, ++it) {
+                const int s = it % kGStages;
+                const uint32_t round = it / kGStages;
+                if (!mbar_wait_bounded(&t_full[s], round & 1, abort_flag, p.status)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t* trw = reinterpret_cast<const uint32_t*>(stage_t(s, dmat, dkt));
+                uint8_t* bt = stage_b(s, dmat);
+#pragma unroll 2
+                for (int j = 0; j < ntn; ++j) {
+                    const int nt = nt0 + j;
+                    const uint32_t* tw = trw + nt * kTileWords;
+                    uint32_t b[4];
+                    decode_lane_u(tw[lw.q0], tw[lw.q1], tw[lw.q2], lw.r8, k16, b);
+                    // B operand row n (feature), K-major 128B-swizzled: element (n, k) at
+                    // (n/8)*1024 + (n%8)*128 + ((2k/16) ^ (n%8))*16 + (2k)%16
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int n = nt * 16 + c0 + ((q >> 1) << 3);
+                        const int k = dkt * 16 + r0 + ((q & 1) << 3);
+                        const int chunk = (k >> 3) ^ (n & 7);
+                        *reinterpret_cast<uint32_t*>(bt + (n >> 3) * 1024 + (n & 7) * 128 + chunk * 16 + (k & 7) * 2) = b[q];
+                    }
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&b_full[s]);
+            }
+            if (!ok) break;
+            // ------------------------------- epilogue -------------------------------
+            if (!mbar_wait_bounded(acc_full, units_done & 1, abort_flag, p.status)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int ept = MODE == 0 ? 1 : 2;  // M tiles per warp
+            for (int ei = 0; ei < ept; ++ei) {
+                const int mt = MODE == 0 ? d / 4 : d / 4 + 2 * ei;
+                const int row = mt * kBM + quarter * 32 + lane;
+                const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+                if (mt * kBM >= rows) continue;  // whole M tile empty (warp-uniform)
+                float v[128];
+                if (MODE == 0) {
+                    const uint32_t colg = (uint32_t)((mt * 2 + 0) * kBN), colu = (uint32_t)((mt * 2 + 1) * kBN);
+                    const __half* svg = p.svh_a + (size_t)e * 2 * p.N + fb * kBN;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float t[32];
+                        tmem_ld32(lane_addr + colg + q * 32, t);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[q * 32 + i] = t[i];
+                    }
+                    out_block128(v, svg);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float t[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) t[i] = v[q * 32 + i];
+                        tmem_st32(lane_addr + colg + q * 32, t);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float t[32];
+                        tmem_ld32(lane_addr + colu + q * 32, t);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[q * 32 + i] = t[i];
+                    }
+                    out_block128(v, svg + p.N);
+                    const __half* sd = p.suh_d + (size_t)e * p.N + fb * kBN;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float g[32];
+                        tmem_ld32(lane_addr + colg + q * 32, g);
+#pragma unroll
+                        for (int c8 = 0; c8 < 4; ++c8) {
+                            float s8[8];
+                            load_half8(sd + q * 32 + c8 * 8, s8);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                const int idx = q * 32 + c8 * 8 + i;
+                                v[idx] = __fmul_rn(r16(act_gu(g[c8 * 8 + i], v[idx], p.limit)), s8[i]);
+                            }
+                        }
+                    }
+                    had128_thread(v);
+#pragma unroll
+                    for (int i = 0; i < 128; ++i) v[i] = __fmul_rn(v[i], kHad);
+                } else {
+                    const uint32_t col = (uint32_t)(mt * kBN);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float t[32];
+                        tmem_ld32(lane_addr + col + q * 32, t);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[q * 32 + i] = t[i];
+                    }
+                    out_block128(v, p.svh_a + (size_t)e * p.N + fb * kBN);
+                }
+                if (row < rows) {
+                    uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(row0 + row) * p.N + fb * kBN);
+#pragma unroll
+                    for (int c8 = 0; c8 < 16; ++c8) {
+                        uint4 o;
+                        o.x = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 0], v[c8 * 8 + 1]));
+                        o.y = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 2], v[c8 * 8 + 3]));
+                        o.z = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 4], v[c8 * 8 + 5]));
+                        o.w = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 6], v[c8 * 8 + 7]));
+                        dst[c8] = o;
+                    }
+                }
+            }
+            tc_fence_before();
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// plan: row passes of the busy experts (gate/up 256 rows, down 512 rows)
+// ---------------------------------------------------------------------------------------------
+__global__ void gemm_plan_kernel(const int* fat_experts, const int* n_fat, const int* counts, const int* offsets,
+                                 int4* passes0, int* n0, int4* passes1, int* n1)
+{
+    if (threadIdx.x != 0) return;
+    const int nf = *n_fat;
+    int a = 0, b = 0;
+    for (int i = 0; i < nf; ++i) {
+        const int e = fat_experts[i], R = counts[e], r0 = offsets[e];
+        for (int r = 0; r < R; r += GemmCfg<0>::rows_per_pass)
+            passes0[a++] = make_int4(e, r0 + r, min(GemmCfg<0>::rows_per_pass, R - r), 0);
+        for (int r = 0; r < R; r += GemmCfg<1>::rows_per_pass)
+            passes1[b++] = make_int4(e, r0 + r, min(GemmCfg<1>::rows_per_pass, R - r), 0);
+    }
+    *n0 = a;
+    *n1 = b;
+}
+
+// passes = sum over busy experts of ceil(rows / rp) <= N / rp + (number of experts, <= min(N, kMaxExperts))
+static int max_passes(int N, int /*E*/, int rp) { return N / rp + (N < kMaxExperts ? N : kMaxExperts) + 1; }
+
+size_t gemm_scratch_bytes(int N, int E, int H, int I)
+{
+    return (size_t)(max_passes(N, E, GemmCfg<0>::rows_per_pass) + max_passes(N, E, GemmCfg<1>::rows_per_pass)) * 16 + 256;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// [rows][K] fp16 rows, box 64 (k) x 128 (rows), 128-byte swizzle, zero fill out of bounds
+static cudaError_t make_map(CUtensorMap* m, const void* base, int rows, int K)
+{
+    auto fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)(rows > 0 ? rows : 1)};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+template <int MODE>
+static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
+{
+    using Cfg = GemmCfg<MODE>;
+    const int H = a.layer->hidden, I = a.layer->intermediate, E = a.layer->num_experts;
+    const int N = a.rows_bound;
+    int4* passes0 = reinterpret_cast<int4*>(a.scratch + 256);
+    int4* passes1 = passes0 + max_passes(N, E, GemmCfg<0>::rows_per_pass);
+    int* counters = reinterpret_cast<int*>(a.scratch);
+    cudaError_t err;
+    if (MODE == 0) {
+        gemm_plan_kernel<<<1, 32, 0, st>>>(a.fat_experts, a.n_fat, a.counts, a.offsets, passes0, counters, passes1,
+                                           counters + 1);
+        if ((err = cudaGetLastError()) != cudaSuccess) return err;
+    }
+    GemmParams p{};
+    if (MODE == 0) {
+        if ((err = make_map(&p.tm_a, a.xt_g, N, H)) != cudaSuccess) return err;
+        if ((err = make_map(&p.tm_b, a.xt_u, N, H)) != cudaSuccess) return err;
+        p.passes = passes0;
+        p.n_passes = counters;
+        p.tab_a = a.layer->gate_ptrs;
+        p.tab_b = a.layer->up_ptrs;
+        p.svh_a = static_cast<const __half*>(a.layer->w13_svh);
+        p.suh_d = static_cast<const __half*>(a.layer->w2_suh);
+        p.out = a.xt_d;
+        p.K = H;
+        p.N = I;
+    } else {
+        if ((err = make_map(&p.tm_a, a.xt_d, N, I)) != cudaSuccess) return err;
+        p.tm_b = p.tm_a;
+        p.passes = passes1;
+        p.n_passes = counters + 1;
+        p.tab_a = a.layer->down_ptrs;
+        p.tab_b = nullptr;
+        p.svh_a = static_cast<const __half*>(a.layer->w2_svh);
+        p.suh_d = nullptr;
+        p.out = a.y;
+        p.K = I;
+        p.N = H;
+    }
+    p.status = a.status;
+    p.limit = a.limit;
+    p.k16 = 65536u;
+    const size_t smem = Cfg::smem_bytes;
+    if ((err = cudaFuncSetAttribute((const void*)exl3_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)smem)) != cudaSuccess)
+        return err;
+    const int units_bound = max_passes(N, E, Cfg::rows_per_pass) * (p.N / kBN);
+    int grid = num_sms();
+    if (units_bound < grid) grid = units_bound;
+    if (grid < 1) grid = 1;
+    exl3_gemm_kernel<MODE><<<grid, kGemmThreads, smem, st>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_gateup(const GemmArgs& a, cudaStream_t st) { return launch_mode<0>(a, st); }
+cudaError_t launch_gemm_down(const GemmArgs& a, cudaStream_t st) { return launch_mode<1>(a, st); }
 
 }  // namespace dsv41

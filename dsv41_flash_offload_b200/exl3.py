@@ -36,8 +36,9 @@ def _env_int(name: str, default: int) -> int:
 
 
 # experts with more rows than this go to the tensor-core grouped GEMM (VLLM_EXL3_FAT_THRESHOLD,
-# patch:146; 32 deployed by the reference's entrypoint). -1 keeps every expert on the GEMV.
-FAT_EXPERT_THRESHOLD = _env_int("VLLM_EXL3_FAT_THRESHOLD", -1)
+# patch:146; 32 deployed by the reference's entrypoint, docker/entrypoint.sh:69). -1 keeps every
+# expert on the decode GEMV.
+FAT_EXPERT_THRESHOLD = _env_int("VLLM_EXL3_FAT_THRESHOLD", 32)
 
 def _rows2d(t: torch.Tensor, T: int) -> torch.Tensor:
     """[T, k] view of a routing tensor given as [T, k] or flat [T*k] (also for T == 0)."""

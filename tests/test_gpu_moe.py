@@ -89,6 +89,41 @@ def test_many_rows_per_expert_vs_oracle(oracle, layer_small):
     assert_close_layer(out.cpu().numpy(), ref, "many rows")
 
 
+def test_gemm_path_small_vs_oracle(oracle, layer_small):
+    """Busy experts (> 32 rows) through the decode-to-smem tcgen05 GEMM, several M tiles each."""
+    T, H, E, k = 300, 512, 16, 4
+    x, ids, w = _inputs(41, T, H, E, k, kind="zipf", zipf_s=1.5)
+    counts = torch.bincount(ids.reshape(-1), minlength=E)
+    assert int((counts > 32).sum()) >= 4 and int(counts.max()) > 256
+    out = exl3.apply_exl3_fused_moe(x, ids, w, layer_small, None, None, LIMIT, fat_threshold=32)
+    assert exl3.read_status(device=DEV) == 0
+    ref = oracle_out(oracle, layer_small, x, ids, w, LIMIT)
+    assert_close_layer(out.cpu().numpy(), ref, "gemm small")
+
+
+def test_gemm_path_full_shape_vs_oracle(oracle, layer_full):
+    """BASELINE layer shape, four busy experts with 160 rows each (two M tiles, one pass)."""
+    T, k = 160, 4
+    experts = torch.tensor([5, 77, 200, 383])
+    g = torch.Generator().manual_seed(0)
+    ids = torch.stack([experts[torch.randperm(4, generator=g)] for _ in range(T)]).to(DEV)
+    w = torch.softmax(torch.randn(T, k, generator=g), 1).to(DEV)
+    x = torch.from_numpy(synth.hidden_np(42, T, 4096)).to(DEV, torch.bfloat16)
+    out = exl3.apply_exl3_fused_moe(x, ids, w, layer_full, None, None, LIMIT, fat_threshold=32)
+    assert exl3.read_status(device=DEV) == 0
+    ref = oracle_out(oracle, layer_full, x, ids, w, LIMIT)
+    assert_close_layer(out.cpu().numpy(), ref, "gemm full shape")
+
+
+def test_gemm_matches_gemv_on_prefill(layer_full):
+    """Prefill chunk (2048 tokens, Zipf 1.1): tensor-core path for busy experts vs all-GEMV."""
+    x, ids, w = _inputs(43, 2048, 4096, 384, kind="zipf", zipf_s=1.1)
+    a = exl3.apply_exl3_fused_moe(x, ids, w, layer_full, None, None, LIMIT, fat_threshold=32)
+    b = exl3.apply_exl3_fused_moe(x, ids, w, layer_full, None, None, LIMIT, fat_threshold=-1)
+    assert exl3.read_status(device=DEV) == 0
+    assert_close_layer(a.cpu().numpy(), b.cpu().numpy(), "gemm vs gemv")
+
+
 def test_input_dtypes_agree(layer_small):
     T, H, E = 9, 512, 16
     x, ids, w = _inputs(12, T, H, E, 4)
