@@ -280,7 +280,9 @@ int dsv41_moe_workspace_size(int32_t T, int32_t topk, int32_t num_experts, int32
         return fail(DSV41_E_INVALID, "bad sizes T=%d topk=%d E=%d H=%d I=%d", T, topk, num_experts, hidden,
                     intermediate);
     const int split = opt ? opt->split_k : 0;
-    const int fat = opt ? opt->fat_threshold : -1;
+    // busy experts are only possible with more tokens than the threshold (the reference's
+    // fat_possible = tokens > FAT_EXPERT_THRESHOLD, patch:245); otherwise everything is GEMV
+    const int fat = (opt && opt->fat_threshold >= 0 && T > opt->fat_threshold) ? opt->fat_threshold : -1;
     *bytes = make_layout(T, topk, num_experts, hidden, intermediate, split, fat).total;
     return DSV41_OK;
 }
@@ -299,7 +301,8 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     const dsv41_moe_options dflt{-1, 0.0f, nullptr, 0, 0};
     const dsv41_moe_options& o = opt ? *opt : dflt;
     if (o.expert_map && o.map_len <= 0) return fail(DSV41_E_INVALID, "expert_map given with map_len %d", o.map_len);
-    const Layout L = make_layout(T, topk, E, H, I, o.split_k, o.fat_threshold);
+    const int fat = (o.fat_threshold >= 0 && T > o.fat_threshold) ? o.fat_threshold : -1;  // fat_possible
+    const Layout L = make_layout(T, topk, E, H, I, o.split_k, fat);
     if (workspace_bytes < L.total)
         return fail(DSV41_E_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, L.total);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -308,7 +311,7 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     const PermBuffers pb = perm_buffers(workspace, L);
     int* status = at<int>(workspace, L.status);
     timer_begin(st);
-    if ((err = launch_permute(ids, weights, L.N, topk, E, o.expert_map, o.map_len, o.fat_threshold, pb, st)) !=
+    if ((err = launch_permute(ids, weights, L.N, topk, E, o.expert_map, o.map_len, fat, pb, st)) !=
         cudaSuccess)
         return cuda_fail(err, "permute");
     timer_mark(st, 1);
@@ -322,7 +325,7 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     timer_mark(st, 2);
     if ((err = run_expert_passes(layer, pb, xt_g, xt_u, xt_d, y, at<float>(workspace, L.partials),
                                  at<int>(workspace, L.counters), status, L.split, L.groups_bound, L.N, o.limit,
-                                 o.fat_threshold, at<uint8_t>(workspace, L.gemm), st)) != cudaSuccess)
+                                 fat, at<uint8_t>(workspace, L.gemm), st)) != cudaSuccess)
         return cuda_fail(err, "expert passes");
     if ((err = launch_combine(y, pb.route_pos, weights, T, topk, H, 0, out, st)) != cudaSuccess)
         return cuda_fail(err, "combine");
