@@ -18,7 +18,7 @@ OK, E_INVALID, E_CUDA, E_WORKSPACE = 0, -1, -2, -3
 # exported symbols, in include/dsv41_b200.h order
 SYMBOLS = (
     "dsv41_last_error", "dsv41_abi_version", "dsv41_build_info", "dsv41_moe_workspace_size",
-    "dsv41_moe_forward", "dsv41_permute_workspace_size", "dsv41_permute", "dsv41_combine",
+    "dsv41_moe_forward", "dsv41_moe_forward_noalloc", "dsv41_permute_workspace_size", "dsv41_permute", "dsv41_combine",
     "dsv41_decode_dense", "dsv41_expert_gemm", "dsv41_expert_gemm_workspace_size", "dsv41_read_status",
     "dsv41_set_stage_timing", "dsv41_read_stage_times",
 )
@@ -66,6 +66,9 @@ def load(path: str | None = None):
         L.dsv41_moe_forward.restype = C.c_int
         L.dsv41_moe_forward.argtypes = [C.POINTER(MoeLayer), vp, i32, i32, i64p, vp, i32, C.POINTER(MoeOptions), vp,
                                         vp, C.c_size_t, vp]
+        L.dsv41_moe_forward_noalloc.restype = C.c_int
+        L.dsv41_moe_forward_noalloc.argtypes = [C.POINTER(MoeLayer), vp, i32, i32, i64p, vp, i32, C.POINTER(MoeOptions),
+                                                vp, vp]
         L.dsv41_permute_workspace_size.restype = C.c_size_t
         L.dsv41_permute_workspace_size.argtypes = [i32, i32, i32]
         L.dsv41_permute.restype = C.c_int

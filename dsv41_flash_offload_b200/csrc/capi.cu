@@ -30,6 +30,17 @@ static int fail(int code, const char* fmt, ...)
     return code;
 }
 
+int set_error(int code, const char* fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
 static int cuda_fail(cudaError_t e, const char* what)
 {
     return fail(DSV41_E_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));

@@ -83,4 +83,7 @@ cudaError_t launch_decode_dense(const void* trellis, int k, int n, __half* w, cu
 
 int num_sms();
 
+// record a message for dsv41_last_error() and return `code`
+int set_error(int code, const char* fmt, ...);
+
 }  // namespace dsv41

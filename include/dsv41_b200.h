@@ -100,6 +100,17 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
                       const dsv41_moe_options* opt, float* out, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* dsv41_moe_forward for callers that cannot allocate device memory (no counterpart in the
+ * reference). Same arguments and results as dsv41_moe_forward, minus the workspace: the scratch
+ * is a fixed 32 MiB device array inside this library, held by every GPU that uses it until the
+ * process exits. Requests needing more scratch than that fail with DSV41_E_WORKSPACE and a
+ * message (at E=384 H=4096 I=2048 top-8 it covers decode batches up to 64 tokens). The first
+ * call on a device looks the array up (make it before any stream capture); calls share the array,
+ * so calls that overlap on the GPU race. Allocates nothing. */
+int dsv41_moe_forward_noalloc(const dsv41_moe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
+                              const int64_t* ids, const float* weights, int32_t topk,
+                              const dsv41_moe_options* opt, float* out, void* stream);
+
 /* Routing permutation (bit-exact, stable by (local expert, flat route index)):
  *   counts/offsets [E+1] int64 (index E = invalid-route sentinel), token_sorted/route_sorted
  *   [T*topk] int32, weight_sorted [T*topk] fp32, route_pos [T*topk] int32 (sorted position of
