@@ -138,6 +138,22 @@ class Exl3MoELayer:
         return 3 * (H // 16) * (I // 16) * 96 + (2 * H + 2 * I + I + H) * 2
 
 
+def as_layer(layer) -> Exl3MoELayer:
+    """The Exl3MoELayer for `layer`: itself, or -- for a vLLM FusedMoE layer set up by vllm_exl3's
+    Exl3MoEMethod (w13_trellis/w2_trellis/w13_suh/w13_svh/w2_suh/w2_svh parameters, patch:633-684) --
+    a view of its tensors, built once and cached on the layer as `_dsv41`."""
+    if isinstance(layer, Exl3MoELayer):
+        return layer
+    cached = getattr(layer, "_dsv41", None)
+    if cached is not None:
+        return cached
+    t = lambda name: getattr(layer, name).data if hasattr(getattr(layer, name), "data") else getattr(layer, name)
+    view = Exl3MoELayer(t("w13_trellis"), t("w2_trellis"), t("w13_suh").contiguous(), t("w13_svh").contiguous(),
+                        t("w2_suh").contiguous(), t("w2_svh").contiguous())
+    layer._dsv41 = view
+    return view
+
+
 # --------------------------------------------------------------------------------------------
 # workspaces: one grow-only device buffer per (device, stream); callers that overlap calls on
 # several streams get one each. Graph capture needs the buffer to exist before capture.
@@ -179,6 +195,7 @@ def apply_exl3_fused_moe(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Te
     """Routed-expert MoE forward; returns fp32 [T, H] (see module docstring). `inners` is accepted for
     signature compatibility and unused (the experts come from `layer`)."""
     L = _lib.load()
+    layer = as_layer(layer)
     if x2d.dim() != 2:
         raise ValueError("x2d must be [T, H]")
     T, H = x2d.shape
