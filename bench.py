@@ -199,6 +199,16 @@ def gateup_bytes(ids, T):
     return d * (2 * TILE_BYTES_PER_MATRIX + 2 * I * 2 + I * 2) + rows * 2 * H * 2 + rows * I * 2, d
 
 
+def gateup_bytes_ep(ids_all, lo, hi):
+    """gateup_bytes for the local forward of the rank owning experts [lo, hi) under expert
+    parallelism: distinct routed experts in its range, and the (token, rank) rows it receives."""
+    import numpy as np
+    cat = np.concatenate([i.reshape(-1) for i in ids_all])
+    d = len(np.unique(cat[(cat >= lo) & (cat < hi)]))
+    rows = sum(int(((i >= lo) & (i < hi)).any(axis=1).sum()) for i in ids_all)
+    return d * (2 * TILE_BYTES_PER_MATRIX + 2 * I * 2 + I * 2) + rows * 2 * H * 2 + rows * I * 2, d
+
+
 def layer_bytes(ids, T):
     import numpy as np
     d = len(np.unique(ids))
@@ -316,15 +326,28 @@ def main():
         return
 
     from dsv41_flash_offload_b200 import exl3
-    layers = [exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, layer=l, device=dev) for l in range(a.layers)]
-    host_batches = make_batches(T, a.batches, 1000 + 100 * rank)
+    from dsv41_flash_offload_b200.ep import EPMoE, local_layer_fn
+    e_loc = E // world
+    lo, hi = rank * e_loc, (rank + 1) * e_loc
+    # N > 1: expert parallelism -- this rank holds experts [lo, hi) of every layer and its own tokens
+    layers = [exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, layer=l, device=dev,
+                                          expert_range=(lo, hi) if world > 1 else None) for l in range(a.layers)]
+    eps = [EPMoE(local_layer_fn(lay, LIMIT), E) for lay in layers] if world > 1 else None
+    all_batches = [make_batches(T, a.batches, 1000 + 100 * r) for r in range(world)]
+    host_batches = all_batches[rank]
     batches = to_device(host_batches, dev)
     out = torch.empty(T, H, dtype=torch.float32, device=dev)
     fat = exl3.FAT_EXPERT_THRESHOLD
 
+    def forward(i, x, ids, w, o):
+        if eps is None:
+            exl3.apply_exl3_fused_moe(x, ids, w, layers[i % len(layers)], None, None, LIMIT, out=o)
+        else:
+            o.copy_(eps[i % len(eps)](x, ids, w))
+
     def step(i):
         x, ids, w = batches[i % len(batches)]
-        exl3.apply_exl3_fused_moe(x, ids, w, layers[i % len(layers)], None, None, LIMIT, out=out)
+        forward(i, x, ids, w, out)
 
     uuid = None
     try:
@@ -338,8 +361,21 @@ def main():
 
     # dominant kernel: per-stage events over the same steps
     st = stage_times(step, a.steps, 2)
-    gb = [gateup_bytes(ids, T) for _, ids, _ in host_batches]
-    lb = [layer_bytes(ids, T) for _, ids, _ in host_batches]
+    if world == 1:
+        gb = [gateup_bytes(ids, T) for _, ids, _ in host_batches]
+        lb = [layer_bytes(ids, T) for _, ids, _ in host_batches]
+    else:
+        # what this rank's local forward streams: the distinct experts of [lo, hi) routed by any rank's
+        # tokens in that step, and the (token, rank) rows it receives
+        gb, lb = [], []
+        for b in range(a.batches):
+            ids_all = [all_batches[r][b][1] for r in range(world)]
+            gb.append(gateup_bytes_ep(ids_all, lo, hi))
+            rows = sum(int(((i >= lo) & (i < hi)).any(axis=1).sum()) for i in ids_all)
+            lb.append(gb[-1][1] * EXPERT_BYTES + rows * H * 6 + rows * TOPK * 12)
+    if eps is not None:
+        for e in eps:
+            e.stats = {k: 0 for k in e.stats}
     bytes_gu = statistics.mean(b for b, _ in gb)
     distinct = statistics.mean(d for _, d in gb)
     achieved = bytes_gu / (st["gemv_gateup"] / 1e3) / 1e9
@@ -357,7 +393,7 @@ def main():
         dx.copy_(x, non_blocking=True)
         dids.copy_(ids, non_blocking=True)
         dw.copy_(w, non_blocking=True)
-        exl3.apply_exl3_fused_moe(dx, dids, dw, layers[i % len(layers)], None, None, LIMIT, out=out)
+        forward(i, dx, dids, dw, out)
         out_host.copy_(out, non_blocking=True)
 
     e2e_ms = time_steps(e2e_step, a.steps, a.warmup, dist_on)
@@ -375,7 +411,8 @@ def main():
                    "layers_cycled": a.layers, "routing_batches": a.batches,
                    "l2": "inputs larger than L2: each step streams the distinct routed experts' words "
                          f"(~{statistics.mean(lb) / 1e9:.2f} GB), layers and batches cycled",
-                   "parallelism": f"{world} independent replica(s)" if world > 1 else "single GPU",
+                   "parallelism": (f"expert parallel over {world} GPUs ({e_loc} experts each, {T} tokens per GPU), "
+                                   "NCCL all-to-all dispatch/combine") if world > 1 else "single GPU",
                    "fat_threshold": fat},
         "roofline": {"bound": "hbm", "kernel": "exl3_gemv_kernel<0> (decode-GEMV gate/up + act + down-input)",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
@@ -389,8 +426,17 @@ def main():
         "gpu_launches": a.steps * launches_per_step(T, fat),
         "clocks": clocks,
     }
+    if eps is not None:
+        calls = a.warmup + a.steps  # the e2e pass, counted since the stats were reset
+        sent = sum(e.stats["sent_rows"] for e in eps) / calls
+        a2a = sum(e.stats["a2a_bytes_out"] + e.stats["a2a_bytes_back"] for e in eps) / calls
+        local_ms = sum(v for v in st.values())
+        line["ep"] = {"experts_per_gpu": e_loc, "rows_sent_per_step": round(sent, 1),
+                      "a2a_bytes_per_step": round(a2a), "local_moe_ms": round(local_ms, 5),
+                      "step_ms": round(ms / a.steps, 5),
+                      "a2a_and_dispatch_share": round(max(0.0, 1.0 - local_ms / (ms / a.steps)), 4)}
 
-    if not a.no_sweep:
+    if not a.no_sweep and world == 1:
         sweep = {}
         for Ts in (1, 8, 32, 64):
             hbs = make_batches(Ts, 4, 2000 + Ts)
@@ -411,7 +457,7 @@ def main():
                               "gemv_gateup_hbm_frac": round(gbs / (sst["gemv_gateup"] / 1e3) / 1e9 / hbm, 4)}
         line["sweep"] = sweep
 
-    if not a.no_prefill:
+    if not a.no_prefill and world == 1:
         Tp = 16384
         hp = make_batches(Tp, 1, 3000, kind="zipf", zipf_s=1.1)
         bp = to_device(hp, dev)

@@ -121,15 +121,20 @@ class Exl3MoELayer:
 
     @classmethod
     def synthetic(cls, num_experts: int, hidden: int, intermediate: int, seed: int = 0, layer: int = 0,
-                  device="cuda") -> "Exl3MoELayer":
-        """Random EXL3 3.0-bpw layer (BASELINE's synthetic weights), generated on the device."""
+                  device="cuda", expert_range: tuple | None = None) -> "Exl3MoELayer":
+        """Random EXL3 3.0-bpw layer (BASELINE's synthetic weights), generated on the device.
+        expert_range=(lo, hi) builds only experts lo..hi-1 of the num_experts-expert layer (an
+        expert-parallel shard), bit-identical to those experts of the full layer."""
         E, H, I = num_experts, hidden, intermediate
+        lo, hi = expert_range if expert_range is not None else (0, E)
+        n = hi - lo
         dev = torch.device(device)
-        w13 = torch.empty((E, 2, H // 16, I // 16, 48), dtype=torch.int16, device=dev)
-        w2 = torch.empty((E, I // 16, H // 16, 48), dtype=torch.int16, device=dev)
-        synth.fill_trellis_torch(w13, seed, synth.STREAM_W13, 0, layer)
-        synth.fill_trellis_torch(w2, seed, synth.STREAM_W2, 0, layer)
-        s13, v13, s2, v2 = (torch.from_numpy(a).to(dev) for a in synth.scales_np(seed, E, H, I, layer))
+        w13 = torch.empty((n, 2, H // 16, I // 16, 48), dtype=torch.int16, device=dev)
+        w2 = torch.empty((n, I // 16, H // 16, 48), dtype=torch.int16, device=dev)
+        per13, per2 = w13[0].numel() if n else 0, w2[0].numel() if n else 0
+        synth.fill_trellis_torch(w13, seed, synth.STREAM_W13, lo * per13, layer)
+        synth.fill_trellis_torch(w2, seed, synth.STREAM_W2, lo * per2, layer)
+        s13, v13, s2, v2 = (torch.from_numpy(a[lo:hi].copy()).to(dev) for a in synth.scales_np(seed, E, H, I, layer))
         return cls(w13, w2, s13.contiguous(), v13.contiguous(), s2.contiguous(), v2.contiguous())
 
     def expert_bytes(self) -> int:

@@ -1,0 +1,55 @@
+"""Worker for tests/test_gpu_ep.py (launched with torchrun, one rank per GPU, NCCL).
+
+Each rank holds its shard E/world of a synthetic BASELINE-shape layer and routes its own 64 tokens over
+all global experts; the expert-parallel output (NCCL all-to-all dispatch/combine) must match the
+single-GPU layer (every rank also builds the full layer) within the parity bar."""
+import datetime
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+from conftest import assert_close_layer  # noqa: E402
+from dsv41_flash_offload_b200 import exl3, synth  # noqa: E402
+from dsv41_flash_offload_b200.ep import EPMoE, local_layer_fn  # noqa: E402
+
+E, H, I, K, T = 384, 4096, 2048, 8, 64
+
+
+def main():
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    rank, world = dist.get_rank(), dist.get_world_size()
+    e_loc = E // world
+    shard = exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, device=dev, expert_range=(rank * e_loc, (rank + 1) * e_loc))
+    full = exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, device=dev)
+    ep = EPMoE(local_layer_fn(shard, 10.0), E)
+    for case in range(3):
+        seed = 500 + 10 * case + rank
+        x = torch.from_numpy(synth.hidden_np(seed, T, H)).to(dev, torch.bfloat16)
+        kind = "zipf" if case == 2 else "uniform"
+        ids_np, w_np = synth.routing_np(seed, T, E, K, kind=kind, zipf_s=1.5)
+        ids, w = torch.from_numpy(ids_np).to(dev), torch.from_numpy(w_np).to(dev)
+        if case == 1:
+            ids[0, :] = -1
+            ids[1, 3] = E + 1
+        out = ep(x, ids, w)
+        ref = exl3.apply_exl3_fused_moe(x, ids, w, full, None, None, 10.0)
+        torch.cuda.synchronize()
+        assert_close_layer(out.cpu().numpy(), ref.cpu().numpy(), f"rank {rank} case {case}")
+    assert exl3.read_status(device=dev) == 0
+    dist.barrier()
+    print(f"rank {rank}/{world} ok: sent {ep.stats['sent_rows']} rows, received {ep.stats['recv_rows']}", flush=True)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
