@@ -230,7 +230,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
 }
 
-// 1-D bulk async copy global -> shared, completing on an mbarrier (no multicast)
+// 1-D bulk async copy global -> this CTA's shared memory, completing on an mbarrier
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy)
 {
     asm volatile(

@@ -8,7 +8,7 @@
 //   pass 1 (down):    D [rows x 128 features] = xt_d . W_d; epilogue: out_block -> y (fp16)
 // Work unit = (busy expert, row pass of 256 (gate/up) or 512 (down) rows, 128-feature block).
 // One CTA per SM, 10 warps:
-//   warp 0     producer: TMA (cp.async.bulk.tensor, SWIZZLE_128B, no multicast) of 128-row x 64-k
+//   warp 0     producer: TMA (cp.async.bulk.tensor, SWIZZLE_128B, into this CTA only) of 128-row x 64-k
 //              activation tiles and 1-D bulk copies of the trellis k-rows, 2-stage mbarrier ring
 //   warp 1     TMEM allocator (512 columns) and single-thread tcgen05.mma issuer
 //              (kind::f16, M=128, N=128, K=16, fp32 accumulators in TMEM); tcgen05.commit frees

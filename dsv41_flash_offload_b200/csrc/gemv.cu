@@ -9,7 +9,7 @@
 //
 // Work unit = (row group of <= 16 rows of one expert, column block, K split). A persistent grid
 // of 2 CTAs per SM walks the units. Per CTA: 16 consumer warps + 1 producer warp.
-//   producer: one 1-D bulk async copy (cp.async.bulk, no multicast) per 768/1536-byte trellis
+//   producer: one 1-D bulk async copy (cp.async.bulk, into this CTA only) per 768/1536-byte trellis
 //             k-row segment and per 256-byte activation row into a 4-stage mbarrier ring;
 //             trellis reads carry an L2 evict-first hint (each expert byte is read once).
 //   consumer warp w: owns one 16-column n-tile; per k-tile it loads the two 32-bit window
