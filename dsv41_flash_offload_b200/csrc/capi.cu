@@ -73,7 +73,8 @@ struct Layout {
 
 static int auto_split(int N, int E, int H, int I, int requested)
 {
-    auto fits = [&](int s) { return s >= 1 && (H / 16) % (s * 8) == 0 && (I / 16) % (s * 8) == 0; };
+    const int r = gemv_stage_rows();
+    auto fits = [&](int s) { return s >= 1 && (H / 16) % (s * r) == 0 && (I / 16) % (s * r) == 0; };
     if (requested > 0) return fits(requested) ? requested : 1;
     const int groups = N < E ? (N > 0 ? N : 1) : E;
     const long long units = (long long)groups * (I / 128);

@@ -23,12 +23,30 @@
 
 namespace dsv41 {
 
-constexpr int kConsumerWarps = 16;
+// launch-shape parameters (compile-time; the defaults are the tuned values)
+#ifndef DSV41_GEMV_MIN_BLOCKS
+#define DSV41_GEMV_MIN_BLOCKS 2       // resident CTAs per SM (register budget follows)
+#endif
+#ifndef DSV41_GEMV_STAGE_ROWS
+#define DSV41_GEMV_STAGE_ROWS 16      // k-tile rows per pipeline stage
+#endif
+#ifndef DSV41_GEMV_STAGES
+#define DSV41_GEMV_STAGES 2
+#endif
+// Measured on B200, decode T=64 step: (1 tile/warp, 8 rows, 4 stages) 2.12 ms; (1, 16, 2) 1.98;
+// (2, 8, 4) 1.97; (2, 16, 2) 1.88; 1 CTA/SM or 3 CTAs/SM variants were slower.
+
+#ifndef DSV41_GEMV_TILES_PER_WARP
+#define DSV41_GEMV_TILES_PER_WARP 2   // adjacent n-tiles per consumer warp (they share the A fragment)
+#endif
+
+constexpr int kTilesPerWarp = DSV41_GEMV_TILES_PER_WARP;
+constexpr int kConsumerWarps = 16 / kTilesPerWarp;   // 16 n-tiles per staged k-row
 constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStageRows = 8;          // k-tile rows per stage
-constexpr int kStages = 4;
+constexpr int kStageRows = DSV41_GEMV_STAGE_ROWS;
+constexpr int kStages = DSV41_GEMV_STAGES;
 constexpr int kRowBytes = 1536;        // 16 tiles of one k-row
-constexpr int kXRowStride = 272;       // 8 k-tiles x 16 halves = 256 B, + 16 B pad (ldmatrix banks)
+constexpr int kXRowStride = kStageRows * 32 + 16;  // stage's k-tiles x 16 halves, + 16 B pad (ldmatrix banks)
 constexpr int kXMatBytes = 16 * kXRowStride;
 constexpr int kEpFloats = 4096;
 
@@ -43,6 +61,7 @@ struct GemvSmem {
 };
 
 size_t gemv_smem_bytes() { return sizeof(GemvSmem); }
+int gemv_stage_rows() { return kStageRows; }
 
 __device__ __forceinline__ void out_block4(float (&y)[4], const __half* svh, int lane)
 {
@@ -57,7 +76,7 @@ __device__ __forceinline__ void out_block4(float (&y)[4], const __half* svh, int
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kGemvThreads, 2) exl3_gemv_kernel(const GemvParams p)
+__global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv_kernel(const GemvParams p)
 {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     GemvSmem& S = *reinterpret_cast<GemvSmem*>(smem_raw);
@@ -101,7 +120,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) exl3_gemv_kernel(const GemvPa
                     break;
                 }
                 const int kt0 = s * k_per_split + st * kStageRows;
-                if (lane == 0) mbar_arrive_expect_tx(&S.full[stage], kStageRows * kRowBytes + nmat * rows * 256);
+                if (lane == 0)
+                    mbar_arrive_expect_tx(&S.full[stage], kStageRows * kRowBytes + nmat * rows * kStageRows * 32);
                 __syncwarp();
                 if (MODE == 0) {
                     if (lane < 2 * kStageRows) {
@@ -118,7 +138,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) exl3_gemv_kernel(const GemvPa
                 for (int c = lane; c < nmat * rows; c += 32) {
                     const int m = c / rows, j = c % rows;
                     const __half* src = (m ? p.xb : p.xa) + (size_t)(row0 + j) * p.K + kt0 * 16;
-                    bulk_g2s(S.x[stage][m] + j * kXRowStride, src, 256, &S.full[stage], pol_x);
+                    bulk_g2s(S.x[stage][m] + j * kXRowStride, src, kStageRows * 32, &S.full[stage], pol_x);
                 }
             }
         }
@@ -137,44 +157,56 @@ __global__ void __launch_bounds__(kGemvThreads, 2) exl3_gemv_kernel(const GemvPa
     // ------------------------------ consumer warps ------------------------------
     const LaneWindow lw = lane_window_setup(lane);
     const uint32_t k16 = p.k16;
-    const int mat = MODE == 0 ? (warp >> 3) : 0;
-    const int tile_in_row = warp;  // byte offset warp * 96 inside a staged 1536-byte k-row
+    const int tile0 = warp * kTilesPerWarp;       // first of this warp's adjacent n-tiles (0..15)
+    const int mat = MODE == 0 ? (tile0 >> 3) : 0;  // gate/up pass: tiles 0-7 gate, 8-15 up
     const uint32_t x_lane = ((lane & 7) + ((lane >> 3) & 1) * 8) * kXRowStride + ((lane >> 4) & 1) * 16;
     uint32_t it = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
         const int ucb = u / p.split, cb = ucb % n_cb, g = ucb / n_cb;
         const int4 G = p.groups[g];
         const int e = G.x, row0 = G.y, rows = G.z;
-        float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+        float acc[kTilesPerWarp][2][4];
+#pragma unroll
+        for (int t = 0; t < kTilesPerWarp; ++t)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[t][h][q] = 0.f;
         for (int st = 0; st < stages_per_unit; ++st, ++it) {
             const int stage = it % kStages;
             const uint32_t round = it / kStages;
             mbar_wait_bounded(&S.full[stage], round & 1, &S.abort_flag, p.status);
-            const uint32_t* trow = reinterpret_cast<const uint32_t*>(S.tr[stage]) + tile_in_row * kTileWords;
+            // this warp's tiles sit at byte offset tile * 96 of each staged 1536-byte k-row
+            const uint32_t* trow = reinterpret_cast<const uint32_t*>(S.tr[stage]) + tile0 * kTileWords;
             const uint32_t xaddr = smem_addr(S.x[stage][mat]) + x_lane;
 #pragma unroll
             for (int r = 0; r < kStageRows; ++r) {
-                const uint32_t* tw = trow + r * (kRowBytes / 4);
-                uint32_t b[4];
-                decode_lane_u(tw[lw.q0], tw[lw.q1], tw[lw.q2], lw.r8, k16, b);
                 uint32_t a[4];
                 ldmatrix_x4(a, xaddr + r * 32);
-                mma_16816(acc0, a, b[0], b[1]);
-                mma_16816(acc1, a, b[2], b[3]);
+#pragma unroll
+                for (int t = 0; t < kTilesPerWarp; ++t) {
+                    const uint32_t* tw = trow + r * (kRowBytes / 4) + t * kTileWords;
+                    uint32_t b[4];
+                    decode_lane_u(tw[lw.q0], tw[lw.q1], tw[lw.q2], lw.r8, k16, b);
+                    mma_16816(acc[t][0], a, b[0], b[1]);
+                    mma_16816(acc[t][1], a, b[2], b[3]);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[stage]);
         }
 
         // accumulators -> shared [mat][row][cols]
-        {
-            const int tcol = (MODE == 0 ? (warp & 7) : warp) * 16 + (lane & 3) * 2;
+#pragma unroll
+        for (int t = 0; t < kTilesPerWarp; ++t) {
+            const int tile = tile0 + t;
+            const int tcol = (MODE == 0 ? (tile & 7) : tile) * 16 + (lane & 3) * 2;
             const int r = lane >> 2;
             float* ep = S.ep + (MODE == 0 ? mat * 16 * cols : 0);
-            *reinterpret_cast<float2*>(ep + r * cols + tcol) = make_float2(acc0[0], acc0[1]);
-            *reinterpret_cast<float2*>(ep + (r + 8) * cols + tcol) = make_float2(acc0[2], acc0[3]);
-            *reinterpret_cast<float2*>(ep + r * cols + tcol + 8) = make_float2(acc1[0], acc1[1]);
-            *reinterpret_cast<float2*>(ep + (r + 8) * cols + tcol + 8) = make_float2(acc1[2], acc1[3]);
+            *reinterpret_cast<float2*>(ep + r * cols + tcol) = make_float2(acc[t][0][0], acc[t][0][1]);
+            *reinterpret_cast<float2*>(ep + (r + 8) * cols + tcol) = make_float2(acc[t][0][2], acc[t][0][3]);
+            *reinterpret_cast<float2*>(ep + r * cols + tcol + 8) = make_float2(acc[t][1][0], acc[t][1][1]);
+            *reinterpret_cast<float2*>(ep + (r + 8) * cols + tcol + 8) = make_float2(acc[t][1][2], acc[t][1][3]);
         }
         named_bar_sync(1, kConsumerWarps * 32);
 
@@ -204,9 +236,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) exl3_gemv_kernel(const GemvPa
             named_bar_sync(1, kConsumerWarps * 32);
         }
 
-        // epilogue: warp j transforms row j of the group
-        if (warp < rows) {
-            const int j = warp;
+        // epilogue: warp w transforms rows w, w + kConsumerWarps, ... of the group
+        for (int j = warp; j < rows; j += kConsumerWarps) {
             if (MODE == 0) {
                 float gv[4], uv[4];
 #pragma unroll
@@ -266,7 +297,7 @@ cudaError_t launch_gemv(int mode, const GemvParams& p, int units_bound, cudaStre
     const void* fn = mode == 0 ? (const void*)exl3_gemv_kernel<0> : (const void*)exl3_gemv_kernel<1>;
     cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
-    int grid = 2 * num_sms();
+    int grid = DSV41_GEMV_MIN_BLOCKS * num_sms();
     if (units_bound < grid) grid = units_bound;
     if (grid < 1) grid = 1;
     if (mode == 0)

@@ -70,6 +70,7 @@ struct GemvParams {
 int gemv_units_bound(int groups_bound, int K, int N, int mode, int split);
 int gemv_units_alloc(int groups_bound, int H, int I, int split);
 size_t gemv_smem_bytes();
+int gemv_stage_rows();   // k-tile rows per pipeline stage: a K split must be a multiple of it
 cudaError_t launch_gemv(int mode, const GemvParams& p, int units_bound, cudaStream_t st);
 
 cudaError_t launch_combine(const __half* y, const int* route_pos, const float* w, int T, int topk,
