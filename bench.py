@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--workload", choices=["decode", "ep40", "prefill-ep"], default="decode",
+                    help="decode: BASELINE configs[1] (default); ep40: configs[3] 40-layer stack, 256-token decode "
+                         "batch; prefill-ep: configs[4] 131,072 tokens x 8 layers, Zipf(1.5)")
     return ap.parse_args()
 
 
@@ -282,6 +285,79 @@ def reference_cpu_tier(layer, batches, seconds, T):
 
 
 # ------------------------------------------------------------------------------------------
+def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst, peak_src):
+    """BASELINE configs[3] (ep40) and configs[4] (prefill-ep): a stack of MoE layers, experts sharded
+    E/world per rank (expert parallel, NCCL all-to-all) -- world 1 runs the same stack on one GPU.
+    Total tokens are fixed (strong scaling) and split evenly over the ranks; the next layer's input
+    is the residual x + moe(x)."""
+    import numpy as np
+    import torch
+    from dsv41_flash_offload_b200 import exl3, synth
+    from dsv41_flash_offload_b200.ep import EPMoE, local_layer_fn
+
+    n_layers, total, zipf = (40, 256, None) if kind == "ep40" else (8, 131072, 1.5)
+    T = total // world
+    e_loc = E // world
+    lo, hi = rank * e_loc, (rank + 1) * e_loc
+    layers = [exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, layer=l, device=dev,
+                                          expert_range=(lo, hi) if world > 1 else None) for l in range(n_layers)]
+    eps = [EPMoE(local_layer_fn(lay, LIMIT), E) for lay in layers]
+    g = torch.Generator(device=dev).manual_seed(7000 + rank)
+    x0 = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    routes = []
+    for l in range(n_layers):
+        ids, w = synth.routing_np(9000 + 100 * rank + l, T, E, TOPK, kind="zipf" if zipf else "uniform",
+                                  zipf_s=zipf or 1.1)
+        routes.append((torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev)))
+
+    def step(i):
+        x = x0
+        for l in range(n_layers):
+            ids, w = routes[l]
+            x = (x.float() + eps[l](x, ids, w)).to(torch.bfloat16)
+        return x
+
+    steps, warm = (max(1, min(a.steps, 10)), max(1, min(a.warmup, 2))) if kind == "ep40" else (max(1, min(a.steps, 3)), 1)
+    ms = time_steps(step, steps, warm, dist_on)
+    for e in eps:
+        e.stats = {k: 0 for k in e.stats}
+    st = stage_times(step, 1, 0)  # one step, per-stage times summed over its layers' local forwards
+    local_ms = sum(st.values()) * n_layers   # stage_times averages over calls (n_layers per step)
+    recv = sum(e.stats["recv_rows"] for e in eps)
+    a2a = sum(e.stats["a2a_bytes_out"] + e.stats["a2a_bytes_back"] for e in eps)
+    t = torch.tensor([recv, a2a, local_ms], dtype=torch.float64, device=dev)
+    allv = [torch.zeros_like(t) for _ in range(world)]
+    if dist_on:
+        torch.distributed.all_gather(allv, t)
+    else:
+        allv = [t]
+    rows = [float(v[0]) for v in allv]
+    value = total * steps / (ms / 1e3)
+    line = {"metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": warm, "ms_per_step": round(ms / steps, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 (fp16 operands, fp32 accumulate; EXL3 3-bit weights decoded exactly)",
+            "data": "synthetic (seeded random EXL3 trellis words; N(0,1) bf16 hidden; routing "
+                    + ("Zipf(1.5)" if zipf else "softmax(N(0,1))") + " top-8)",
+            "config": {"workload": (f"BASELINE configs[3]: {n_layers}-layer MoE stack E={E} H={H} I={I} top-{TOPK}, "
+                                    f"decode batch {total} tokens" if kind == "ep40" else
+                                    f"BASELINE configs[4]: {total} tokens through {n_layers} MoE layers, Zipf(1.5) "
+                                    "routing"),
+                       "parallelism": f"expert parallel over {world} GPU(s), {e_loc} experts each, {T} tokens per "
+                                      "GPU, NCCL all-to-all dispatch/combine" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (every step streams the routed experts of all layers)"},
+            "layer_tok_s": round(value * n_layers, 1),
+            "ep": {"rows_per_gpu_per_step": [round(r, 1) for r in rows],
+                   "max_over_mean_rows": round(max(rows) / max(statistics.mean(rows), 1e-9), 3),
+                   "a2a_bytes_per_step": [round(float(v[1])) for v in allv],
+                   "local_moe_ms_per_step": [round(float(v[2]), 3) for v in allv],
+                   "a2a_and_dispatch_share": round(max(0.0, 1.0 - max(float(v[2]) for v in allv) / (ms / steps)), 4)}}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def main():
     a = parse()
     import torch
@@ -324,6 +400,9 @@ def main():
         if dist_on:
             torch.distributed.destroy_process_group()
         return
+
+    if a.workload != "decode":
+        return run_stack_workload(a, a.workload, world, rank, local, dev, dist_on, hbm, tf_burst, peak_src)
 
     from dsv41_flash_offload_b200 import exl3
     from dsv41_flash_offload_b200.ep import EPMoE, local_layer_fn

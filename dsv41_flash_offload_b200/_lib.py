@@ -35,7 +35,7 @@ class MoeLayer(C.Structure):
 
 class MoeOptions(C.Structure):
     _fields_ = [("fat_threshold", C.c_int32), ("limit", C.c_float), ("expert_map", C.c_void_p),
-                ("map_len", C.c_int32), ("split_k", C.c_int32)]
+                ("map_len", C.c_int32), ("split_k", C.c_int32), ("max_routes", C.c_int32)]
 
 
 class Dsv41Error(RuntimeError):

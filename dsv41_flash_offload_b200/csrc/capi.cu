@@ -68,7 +68,7 @@ static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 struct Layout {
     size_t status, counts, offsets, token_sorted, weight_sorted, route_sorted, expert_sorted, route_pos, groups,
         nlists, fat_experts, seg_hist, xt_g, xt_u, xt_d, y, partials, counters, gemm, total;
-    int N, E, H, I, split, groups_bound, units_bound;
+    int N, E, H, I, split, groups_bound, units_bound, rows;
 };
 
 static int auto_split(int N, int E, int H, int I, int requested)
@@ -84,17 +84,20 @@ static int auto_split(int N, int E, int H, int I, int requested)
     return s;
 }
 
-static Layout make_layout(int T, int topk, int E, int H, int I, int split_req, int fat)
+static Layout make_layout(int T, int topk, int E, int H, int I, int split_req, int fat, int max_routes = 0)
 {
     Layout L{};
     L.N = T * topk;
     L.E = E;
     L.H = H;
     L.I = I;
-    L.split = auto_split(L.N, E, H, I, split_req);
-    L.groups_bound = max_groups(L.N, E);
+    // row buffers hold the valid (locally routed) rows only; max_routes bounds them when the caller knows
+    L.rows = (max_routes > 0 && max_routes < L.N) ? max_routes : L.N;
+    L.split = auto_split(L.rows, E, H, I, split_req);
+    L.groups_bound = max_groups(L.rows, E);
     L.units_bound = gemv_units_alloc(L.groups_bound, H, I, L.split);
     const size_t N = (size_t)(L.N > 0 ? L.N : 1), E1 = (size_t)E + 1;
+    const size_t R = (size_t)(L.rows > 0 ? L.rows : 1);
     size_t o = 0;
     auto take = [&](size_t bytes) {
         const size_t at = o;
@@ -113,13 +116,13 @@ static Layout make_layout(int T, int topk, int E, int H, int I, int split_req, i
     L.nlists = take(16);
     L.fat_experts = take(E1 * 4);
     L.seg_hist = take(perm_seg_hist_ints(L.N, E) * 4 + 4);
-    L.xt_g = take(N * H * 2);
-    L.xt_u = take(N * H * 2);
-    L.xt_d = take(N * I * 2);
-    L.y = take(N * H * 2);
+    L.xt_g = take(R * H * 2);
+    L.xt_u = take(R * H * 2);
+    L.xt_d = take(R * I * 2);
+    L.y = take(R * H * 2);
     L.partials = take(L.split > 1 ? (size_t)L.units_bound * 4096 * 4 : 16);
     L.counters = take((size_t)(L.units_bound / L.split + 1) * 4);
-    L.gemm = take(fat >= 0 ? gemm_scratch_bytes(L.N, E, H, I) : 16);
+    L.gemm = take(fat >= 0 ? gemm_scratch_bytes(L.rows, E, H, I) : 16);
     L.total = o;
     return L;
 }
@@ -145,6 +148,9 @@ static PermBuffers perm_buffers(void* ws, const Layout& L)
     pb.n_fat = at<int>(ws, L.nlists) + 1;
     pb.fat_experts = at<int>(ws, L.fat_experts);
     pb.seg_hist = at<int>(ws, L.seg_hist);
+    pb.nrows = at<int>(ws, L.nlists) + 2;
+    pb.status = at<int>(ws, L.status);
+    pb.rows_cap = L.rows;
     return pb;
 }
 
@@ -295,7 +301,9 @@ int dsv41_moe_workspace_size(int32_t T, int32_t topk, int32_t num_experts, int32
     // busy experts are only possible with more tokens than the threshold (the reference's
     // fat_possible = tokens > FAT_EXPERT_THRESHOLD, patch:245); otherwise everything is GEMV
     const int fat = (opt && opt->fat_threshold >= 0 && T > opt->fat_threshold) ? opt->fat_threshold : -1;
-    *bytes = make_layout(T, topk, num_experts, hidden, intermediate, split, fat).total;
+    const int max_routes = opt ? opt->max_routes : 0;
+    if (max_routes < 0) return fail(DSV41_E_INVALID, "max_routes %d < 0", max_routes);
+    *bytes = make_layout(T, topk, num_experts, hidden, intermediate, split, fat, max_routes).total;
     return DSV41_OK;
 }
 
@@ -310,11 +318,12 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     if (T > 0 && (!x || !ids || !weights || !out)) return fail(DSV41_E_INVALID, "NULL input/output pointer");
     if (!workspace) return fail(DSV41_E_INVALID, "workspace is NULL");
     const int E = layer->num_experts, H = layer->hidden, I = layer->intermediate;
-    const dsv41_moe_options dflt{-1, 0.0f, nullptr, 0, 0};
+    const dsv41_moe_options dflt{-1, 0.0f, nullptr, 0, 0, 0};
     const dsv41_moe_options& o = opt ? *opt : dflt;
     if (o.expert_map && o.map_len <= 0) return fail(DSV41_E_INVALID, "expert_map given with map_len %d", o.map_len);
+    if (o.max_routes < 0) return fail(DSV41_E_INVALID, "max_routes %d < 0", o.max_routes);
     const int fat = (o.fat_threshold >= 0 && T > o.fat_threshold) ? o.fat_threshold : -1;  // fat_possible
-    const Layout L = make_layout(T, topk, E, H, I, o.split_k, fat);
+    const Layout L = make_layout(T, topk, E, H, I, o.split_k, fat, o.max_routes);
     if (workspace_bytes < L.total)
         return fail(DSV41_E_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, L.total);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -331,12 +340,12 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     __half* xt_u = at<__half>(workspace, L.xt_u);
     __half* xt_d = at<__half>(workspace, L.xt_d);
     __half* y = at<__half>(workspace, L.y);
-    if ((err = launch_prep(x, x_dtype, pb.token_sorted, pb.expert_sorted, pb.offsets + E, L.N,
+    if ((err = launch_prep(x, x_dtype, pb.token_sorted, pb.expert_sorted, pb.nrows, L.rows,
                            static_cast<const __half*>(layer->w13_suh), H, xt_g, xt_u, st)) != cudaSuccess)
         return cuda_fail(err, "prep");
     timer_mark(st, 2);
     if ((err = run_expert_passes(layer, pb, xt_g, xt_u, xt_d, y, at<float>(workspace, L.partials),
-                                 at<int>(workspace, L.counters), status, L.split, L.groups_bound, L.N, o.limit,
+                                 at<int>(workspace, L.counters), status, L.split, L.groups_bound, L.rows, o.limit,
                                  fat, at<uint8_t>(workspace, L.gemm), st)) != cudaSuccess)
         return cuda_fail(err, "expert passes");
     if ((err = launch_combine(y, pb.route_pos, weights, T, topk, H, 0, out, st)) != cudaSuccess)
@@ -388,6 +397,9 @@ int dsv41_permute(const int64_t* ids, const float* weights, int32_t T, int32_t t
     pb.seg_hist = at<int>(workspace, take(perm_seg_hist_ints(N, num_experts) * 4 + 4));
     pb.counts64 = counts;
     pb.offsets64 = offsets;
+    pb.nrows = pb.n_groups + 2;
+    pb.status = nullptr;
+    pb.rows_cap = N;
     cudaError_t err = launch_permute(ids, weights, N, topk, num_experts, expert_map, map_len, -1, pb,
                                      static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(err, "permute");
@@ -486,6 +498,8 @@ int dsv41_expert_gemm(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     pb.n_groups = at<int>(workspace, offs[6]);
     pb.n_fat = pb.n_groups + 1;
     int* nrows = pb.n_groups + 2;
+    pb.nrows = nrows;
+    pb.rows_cap = total_rows;
     pb.token_sorted = const_cast<int*>(token_sorted);
     pb.weight_sorted = const_cast<float*>(weight_sorted);
     cudaError_t err;

@@ -22,7 +22,7 @@ constexpr uint16_t kKinvBits = 0x1eee;
 constexpr uint16_t kKbiasBits = 0xc931;
 
 // status word codes written by kernels (never a trap)
-enum : int { kStatusOk = 0, kStatusWaitTimeout = 1, kStatusBadShape = 2 };
+enum : int { kStatusOk = 0, kStatusWaitTimeout = 1, kStatusBadShape = 2, kStatusRouteCapacity = 3 };
 
 // ------------------------------------------------------------------------------------------
 // decode

@@ -28,6 +28,9 @@ struct PermBuffers {
     int* seg_hist;       // [nseg][E+1] (multi-CTA path)
     int64_t* counts64;   // optional [E+1] (reference contract, int64)
     int64_t* offsets64;  // optional [E+1]
+    int* nrows;          // [1] sorted rows the expert passes process (valid routes, 0 on overflow)
+    int* status;         // optional status word (route-capacity overflow)
+    int rows_cap;        // capacity of the row buffers (valid routes beyond it: overflow)
 };
 
 size_t perm_seg_hist_ints(int N, int E);

@@ -92,16 +92,18 @@ __device__ void finish_lists(const PermArgs& a, int* tot, int* tmp, int* scratch
         a.pb.offsets[e] = tot[e];
         if (a.pb.offsets64) a.pb.offsets64[e] = tot[e];
     }
+    // more valid routes than the row buffers hold: no expert work at all (status 3, zero output)
+    const bool over = tot[E] > a.pb.rows_cap;
     // row groups of GEMV experts
     for (int e = t; e <= E; e += nt) {
-        const int c = (e < E) ? a.pb.counts[e] : 0;
+        const int c = (e < E && !over) ? a.pb.counts[e] : 0;
         const bool fat = a.fat >= 0 && c > a.fat;
         tmp[e] = (c == 0 || fat) ? 0 : (c + kRowsPerGroup - 1) / kRowsPerGroup;
     }
     __syncthreads();
     const int ng = block_exclusive_scan(tmp, E + 1, scratch);
     for (int e = t; e < E; e += nt) {
-        const int c = a.pb.counts[e];
+        const int c = over ? 0 : a.pb.counts[e];
         const bool fat = a.fat >= 0 && c > a.fat;
         if (c == 0 || fat) continue;
         const int g0 = tmp[e], row0 = tot[e];
@@ -110,25 +112,27 @@ __device__ void finish_lists(const PermArgs& a, int* tot, int* tmp, int* scratch
     }
     __syncthreads();
     for (int e = t; e <= E; e += nt) {
-        const int c = (e < E) ? a.pb.counts[e] : 0;
+        const int c = (e < E && !over) ? a.pb.counts[e] : 0;
         tmp[e] = (a.fat >= 0 && c > a.fat) ? 1 : 0;
     }
     __syncthreads();
     const int nf = block_exclusive_scan(tmp, E + 1, scratch);
     for (int e = t; e < E; e += nt) {
-        const int c = a.pb.counts[e];
+        const int c = over ? 0 : a.pb.counts[e];
         if (a.fat >= 0 && c > a.fat) a.pb.fat_experts[tmp[e]] = e;
     }
     if (t == 0) {
         *a.pb.n_groups = ng;
         *a.pb.n_fat = nf;
+        if (a.pb.nrows) *a.pb.nrows = over ? 0 : tot[E];
+        if (over && a.pb.status) atomicExch(a.pb.status, kStatusRouteCapacity);
     }
 }
 
 // Walk this warp's segment [b, e) in order; `row` is the warp's per-expert counter row in
 // shared memory. Histogram mode adds counts; scatter mode assigns positions base + rank.
 template <bool SCATTER>
-__device__ void walk_segment(const PermArgs& a, int b, int e, int* row, const int* off)
+__device__ void walk_segment(const PermArgs& a, int b, int e, int* row, const int* off, bool drop = false)
 {
     const int lane = threadIdx.x & 31;
     for (int i0 = b; i0 < e; i0 += 32) {
@@ -151,7 +155,7 @@ __device__ void walk_segment(const PermArgs& a, int b, int e, int* row, const in
                 a.pb.weight_sorted[pos] = a.w ? a.w[i] : 0.0f;
                 a.pb.route_sorted[pos] = i;
                 a.pb.expert_sorted[pos] = l;
-                a.pb.route_pos[i] = (l == a.E) ? -1 : pos;
+                a.pb.route_pos[i] = (l == a.E || drop) ? -1 : pos;
                 if (lane == leader) row[l] += __popc(peers);
             }
         }
@@ -188,7 +192,7 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const PermArgs a)
     __syncthreads();
     finish_lists(a, tot, tmp, scratch);  // tot becomes offsets
     __syncthreads();
-    walk_segment<true>(a, b, e, row, tot);
+    walk_segment<true>(a, b, e, row, tot, tot[a.E] > a.pb.rows_cap);
 }
 
 // Multi-CTA path: (1) per-segment histograms, (2) one CTA scans, (3) stable scatter.
@@ -247,7 +251,7 @@ __global__ void __launch_bounds__(kPermWarps * 32) permute_scatter_kernel(const 
         for (int x = lane; x < E1; x += 32) row[x] = a.pb.seg_hist[(size_t)sg * E1 + x];
     __syncthreads();
     const int b = min(a.N, sg * kPermSegment), e = min(a.N, b + kPermSegment);
-    walk_segment<true>(a, b, e, row, off);
+    walk_segment<true>(a, b, e, row, off, off[a.E] > a.pb.rows_cap);
 }
 
 // Work lists for a caller-given expert list over caller-permuted rows (run_batch semantics).

@@ -62,6 +62,9 @@ class EPMoE:
             return self.expert_fn(x2d, torch.where((ids >= 0) & (ids < self.E), ids, torch.full_like(ids, -1)), weights)
         tok, dst, counts, dest = self.plan(ids)
         k = ids.shape[1]
+        # routes (not rows) per destination: the receiver sizes its local forward by them
+        routes = torch.bincount(dest[dest >= 0], minlength=self.world)[: self.world]
+        counts = torch.stack([counts, routes], 1).reshape(-1)           # [world * 2]
         # metadata of each sent row: local expert ids of the routes owned by the destination (-1 otherwise)
         r_ids = ids[tok]
         own = dest[tok] == dst.unsqueeze(1)
@@ -71,14 +74,16 @@ class EPMoE:
         # counts exchange, then the host-visible split sizes
         recv_counts = torch.empty_like(counts)
         dist.all_to_all_single(recv_counts, counts.contiguous(), group=self.group)
-        sc = counts.tolist()
-        rc = recv_counts.tolist()
+        both = torch.stack([counts, recv_counts]).tolist()              # one host sync
+        sc, rc = both[0][0::2], both[1][0::2]
+        recv_routes = int(sum(both[1][1::2]))
         R = int(sum(rc))
         recv = torch.empty((R, H), dtype=x2d.dtype, device=x2d.device)
         recv_meta = torch.empty((R, 2 * k), dtype=torch.int32, device=x2d.device)
         dist.all_to_all_single(recv, send, rc, sc, group=self.group)
         dist.all_to_all_single(recv_meta, meta, rc, sc, group=self.group)
-        part = self.expert_fn(recv, recv_meta[:, :k].to(torch.int64), recv_meta[:, k:].contiguous().view(torch.float32))
+        part = self.expert_fn(recv, recv_meta[:, :k].to(torch.int64), recv_meta[:, k:].contiguous().view(torch.float32),
+                              max_routes=recv_routes)
         back = torch.empty((send.shape[0], H), dtype=torch.float32, device=x2d.device)
         dist.all_to_all_single(back, part.contiguous(), sc, rc, group=self.group)
         out = torch.zeros((T, H), dtype=torch.float32, device=x2d.device)
@@ -94,9 +99,10 @@ def local_layer_fn(layer, limit: float | None = 10.0, fat_threshold: int | None 
     """expert_fn running this rank's experts through the B200 kernels (apply_exl3_fused_moe)."""
     from .exl3 import apply_exl3_fused_moe
 
-    def fn(x, local_ids, w):
+    def fn(x, local_ids, w, max_routes=0):
         if x.shape[0] == 0:
             return torch.zeros((0, x.shape[1]), dtype=torch.float32, device=x.device)
-        return apply_exl3_fused_moe(x, local_ids, w, layer, None, None, limit, fat_threshold=fat_threshold)
+        return apply_exl3_fused_moe(x, local_ids, w, layer, None, None, limit, fat_threshold=fat_threshold,
+                                    max_routes=max_routes)
 
     return fn

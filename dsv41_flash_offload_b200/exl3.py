@@ -195,7 +195,7 @@ def _stream_ptr(s: torch.cuda.Stream):
 
 def apply_exl3_fused_moe(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, layer: Exl3MoELayer,
                          inners=None, expert_map: torch.Tensor | None = None, limit: float | None = None,
-                         *, fat_threshold: int | None = None, split_k: int = 0,
+                         *, fat_threshold: int | None = None, split_k: int = 0, max_routes: int = 0,
                          out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Routed-expert MoE forward; returns fp32 [T, H] (see module docstring). `inners` is accepted for
     signature compatibility and unused (the experts come from `layer`)."""
@@ -225,7 +225,7 @@ def apply_exl3_fused_moe(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Te
     if expert_map is not None:
         emap = expert_map.to(device=dev, dtype=torch.int32).contiguous()
     opt = _lib.MoeOptions(fat, lim, emap.data_ptr() if emap is not None else None,
-                          emap.numel() if emap is not None else 0, split_k)
+                          emap.numel() if emap is not None else 0, split_k, int(max_routes))
     stream = torch.cuda.current_stream(dev)
     nbytes = C.c_size_t()
     _lib.check(L.dsv41_moe_workspace_size(T, topk, layer._exl3_num_experts, H, layer._exl3_intermediate_local,

@@ -79,7 +79,11 @@ typedef struct dsv41_moe_options {
     float limit;
     const int32_t* expert_map;
     int32_t map_len;
-    int32_t split_k; /* 0 = automatic */
+    int32_t split_k;    /* 0 = automatic */
+    int32_t max_routes; /* upper bound on routes with a valid local expert; row buffers are sized by it
+                           (0 = T*topk). A call with more valid routes drops them all, writes zeros and
+                           sets status 3 (see dsv41_read_status). Used by expert-parallel callers whose
+                           rows carry mostly non-local route slots. */
 } dsv41_moe_options;
 
 /* Last error message of the calling thread ("" if none). */
@@ -142,7 +146,7 @@ int dsv41_expert_gemm_workspace_size(int32_t total_rows, int32_t n_experts, int3
                                      int32_t intermediate, size_t* bytes);
 
 /* Synchronise `stream` and return the device status word of a workspace (0 = ok,
- * 1 = a bounded device wait ran out), then clear it. */
+ * 1 = a bounded device wait ran out, 3 = more valid routes than options.max_routes), then clear it. */
 int dsv41_read_status(const void* workspace, void* stream, int32_t* status);
 
 /* Profiling (no counterpart in the reference; used by bench.py to time each kernel on the stream

@@ -51,7 +51,9 @@ def _worker(rank, world, port, case, q):
     try:
         e_loc = E // world
 
-        def expert_fn(xr, local_ids, wr):
+        def expert_fn(xr, local_ids, wr, max_routes=0):
+            if max_routes:
+                assert int((local_ids >= 0).sum()) == max_routes
             glob = torch.where(local_ids >= 0, local_ids + rank * e_loc, torch.full_like(local_ids, -1))
             assert bool(((local_ids >= -1) & (local_ids < e_loc)).all())
             scale = torch.where(glob >= 0, wr * (glob + 1).float(), torch.zeros_like(wr)).sum(1, keepdim=True)

@@ -124,6 +124,23 @@ def test_gemm_matches_gemv_on_prefill(layer_full):
     assert_close_layer(a.cpu().numpy(), b.cpu().numpy(), "gemm vs gemv")
 
 
+def test_max_routes_bound(layer_small):
+    """Row buffers sized by a caller bound on valid routes (expert-parallel receivers): an exact bound
+    gives the same output; a bound that is too small drops the call (zeros) and sets status 3."""
+    T, H, E, k = 40, 512, 16, 4
+    x, ids, w = _inputs(51, T, H, E, k)
+    ids[(torch.arange(T * k, device=DEV).reshape(T, k) % 3) == 0] = -1
+    nvalid = int((ids >= 0).sum())
+    ref = exl3.apply_exl3_fused_moe(x, ids, w, layer_small, None, None, LIMIT)
+    a = exl3.apply_exl3_fused_moe(x, ids, w, layer_small, None, None, LIMIT, max_routes=nvalid)
+    assert torch.equal(a, ref)
+    assert exl3.read_status(device=DEV) == 0
+    b = exl3.apply_exl3_fused_moe(x, ids, w, layer_small, None, None, LIMIT, max_routes=nvalid - 1)
+    assert float(b.abs().max()) == 0.0
+    assert exl3.read_status(device=DEV) == 3
+    assert exl3.read_status(device=DEV) == 0
+
+
 def test_input_dtypes_agree(layer_small):
     T, H, E = 9, 512, 16
     x, ids, w = _inputs(12, T, H, E, 4)
