@@ -302,6 +302,9 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
     layers = [exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, layer=l, device=dev,
                                           expert_range=(lo, hi) if world > 1 else None) for l in range(n_layers)]
     eps = [EPMoE(local_layer_fn(lay, LIMIT), E) for lay in layers]
+    if kind == "ep40":
+        for ep in eps:
+            ep.slot_capacity = T  # decode batches: fixed-slot dispatch, no host synchronisation
     g = torch.Generator(device=dev).manual_seed(7000 + rank)
     x0 = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
     routes = []
@@ -412,6 +415,8 @@ def main():
     layers = [exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, layer=l, device=dev,
                                           expert_range=(lo, hi) if world > 1 else None) for l in range(a.layers)]
     eps = [EPMoE(local_layer_fn(lay, LIMIT), E) for lay in layers] if world > 1 else None
+    for ep in eps or []:
+        ep.slot_capacity = T  # every rank runs T-token decode batches: fixed-slot dispatch
     all_batches = [make_batches(T, a.batches, 1000 + 100 * r) for r in range(world)]
     host_batches = all_batches[rank]
     batches = to_device(host_batches, dev)

@@ -60,6 +60,50 @@ class EPMoE:
         weights = weights.reshape(T, ids.shape[1]).to(torch.float32)
         if self.world == 1:
             return self.expert_fn(x2d, torch.where((ids >= 0) & (ids < self.E), ids, torch.full_like(ids, -1)), weights)
+        if 0 < T <= self.slot_capacity:
+            return self._fixed_slots(x2d, ids, weights)
+        return self._compact(x2d, ids, weights)
+
+    # Fixed-slot dispatch for small batches: every rank pads its batch to the same `slot_capacity`
+    # tokens (all ranks must use the same value, e.g. the largest decode batch a serving engine
+    # captures) and every token gets a slot in every destination's block, so all split sizes are
+    # equal and known: no host synchronisation (CUDA-graph capturable). The padding costs
+    # slot_capacity * world rows of traffic, negligible at decode batch sizes. 0 = always compact.
+    slot_capacity = 0
+
+    def _fixed_slots(self, x2d, ids, weights):
+        T0, H = x2d.shape
+        k = ids.shape[1]
+        T = self.slot_capacity
+        if T0 < T:  # pad with tokens that have no route
+            x2d = torch.cat([x2d, torch.zeros((T - T0, H), dtype=x2d.dtype, device=x2d.device)])
+            ids = torch.cat([ids, torch.full((T - T0, k), -1, dtype=ids.dtype, device=ids.device)])
+            weights = torch.cat([weights, torch.zeros((T - T0, k), dtype=weights.dtype, device=weights.device)])
+        valid = (ids >= 0) & (ids < self.E)
+        dest = torch.where(valid, ids // self.E_loc, torch.full_like(ids, -1))
+        ranks = torch.arange(self.world, device=ids.device).view(self.world, 1, 1)
+        own = dest.unsqueeze(0) == ranks                                   # [world, T, k]
+        local = torch.where(own, ids.unsqueeze(0) - ranks * self.E_loc, torch.full_like(own, -1, dtype=torch.int64))
+        meta = torch.cat([local.to(torch.int32), weights.unsqueeze(0).expand(self.world, T, k).view(torch.int32)], 2)
+        send = x2d.unsqueeze(0).expand(self.world, T, H).contiguous()
+        recv = torch.empty_like(send)
+        recv_meta = torch.empty_like(meta)
+        dist.all_to_all_single(recv.view(self.world * T, H), send.view(self.world * T, H), group=self.group)
+        dist.all_to_all_single(recv_meta.view(self.world * T, 2 * k), meta.contiguous().view(self.world * T, 2 * k),
+                               group=self.group)
+        rm = recv_meta.view(self.world * T, 2 * k)
+        part = self.expert_fn(recv.view(self.world * T, H), rm[:, :k].to(torch.int64),
+                              rm[:, k:].contiguous().view(torch.float32))
+        back = torch.empty((self.world, T, H), dtype=torch.float32, device=x2d.device)
+        dist.all_to_all_single(back.view(self.world * T, H), part.contiguous(), group=self.group)
+        self.stats["sent_rows"] += self.world * T
+        self.stats["recv_rows"] += self.world * T
+        self.stats["a2a_bytes_out"] += int(send.numel() * send.element_size() + meta.numel() * 4)
+        self.stats["a2a_bytes_back"] += int(back.numel() * 4)
+        return back.sum(0)[:T0]
+
+    def _compact(self, x2d, ids, weights):
+        T, H = x2d.shape
         tok, dst, counts, dest = self.plan(ids)
         k = ids.shape[1]
         # routes (not rows) per destination: the receiver sizes its local forward by them

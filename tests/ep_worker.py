@@ -32,7 +32,9 @@ def main():
     shard = exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, device=dev, expert_range=(rank * e_loc, (rank + 1) * e_loc))
     full = exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, device=dev)
     ep = EPMoE(local_layer_fn(shard, 10.0), E)
-    for case in range(3):
+    for case in range(6):
+        ep.slot_capacity = 96 if case >= 3 else 0   # compact dispatch, then fixed slots
+        case %= 3
         seed = 500 + 10 * case + rank
         x = torch.from_numpy(synth.hidden_np(seed, T, H)).to(dev, torch.bfloat16)
         kind = "zipf" if case == 2 else "uniform"

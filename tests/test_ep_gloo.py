@@ -45,7 +45,7 @@ def _reference(x, ids, w):
     return scale * x
 
 
-def _worker(rank, world, port, case, q):
+def _worker(rank, world, port, case, q, fixed_slots):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -60,6 +60,7 @@ def _worker(rank, world, port, case, q):
             return scale * xr
 
         ep = EPMoE(expert_fn, E)
+        ep.slot_capacity = 16 if fixed_slots else 0   # both dispatch modes (T = 13 + rank <= 16)
         x, ids, w = _inputs(rank, case)
         out = ep(x, ids, w)
         err = float((out - _reference(x, ids, w)).abs().max())
@@ -68,12 +69,13 @@ def _worker(rank, world, port, case, q):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("fixed_slots", [False, True])
 @pytest.mark.parametrize("world,case", [(2, 0), (2, 1), (2, 2), (4, 0), (4, 2)])
-def test_ep_dispatch_combine_gloo(world, case):
+def test_ep_dispatch_combine_gloo(world, case, fixed_slots):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q, fixed_slots)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
