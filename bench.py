@@ -9,7 +9,7 @@ clamp 10) over one batch: the headline workload is BASELINE configs[1]'s decode 
 with uniform top-8 routing (all 384 experts HBM-resident). Synthetic seeded inputs stand in for real
 weights (no checkpoint): uniform random trellis words, +-1 suh, U(0.5,1.5)/64 svh, N(0,1) bf16
 hidden states, softmax(N(0,1)) top-8 routing. Layers and routing batches are cycled so every step
-streams ~2.7 GB of expert words (inputs far larger than the 126 MB L2).
+streams ~1.7 GB of distinct routed experts' words (inputs far larger than the 126 MB L2).
 
 value   = tokens of all ranks / max-over-ranks device time of K steps (inputs resident in HBM)
 e2e     = the same through apply_exl3_fused_moe with pinned host inputs: H2D of x/ids/weights and
@@ -21,7 +21,9 @@ roofline= the dominant kernel (decode-GEMV gate/up pass): algorithmic bytes (dis
 cpu_baseline / --impl reference = the reference's own AVX2 CPU expert tier
           (kernels/cpu_avx2/ft_tier_ext.cpp tier_forward, built into oracle/_ref) on the same
           decode batches, all host cores, rank 0 only.
-N > 1 runs independent replicas (weak scaling; the expert-parallel path is a separate workload).
+N > 1 (torchrun, one rank per GPU) runs the expert-parallel layer: each rank holds E/N experts and
+its own 64-token batch (weak scaling); fixed-slot NCCL all-to-all dispatch/combine, no host sync.
+--workload ep40 / prefill-ep run BASELINE configs[3] / configs[4] instead (strong scaling).
 """
 from __future__ import annotations
 
@@ -41,7 +43,24 @@ E, H, I, TOPK = 384, 4096, 2048, 8
 LIMIT = 10.0
 METRIC = "MoE-layer tok/s (decode B=64, prefill 16k) @1/2/4/8 B200; % HBM/tensor peak"
 TILE_BYTES_PER_MATRIX = (H // 16) * (I // 16) * 96          # 3,145,728
-EXPERT_BYTES = 3 * TILE_BYTES_PER_MATRIX + (2 * H + 2 * I + I + H) * 2   # 9,474,048
+EXPERT_BYTES = 3 * TILE_BYTES_PER_MATRIX + (2 * H + 2 * I + I + H) * 2   # 9,474,048 (3 weight matrices + suh/svh)
+
+
+def claim_stdout():
+    """Route everything written to file descriptor 1 (NCCL prints its version banner there with printf)
+    to stderr, and return a writer for the saved stdout so the result line is the only thing on it."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    out = os.fdopen(saved, "w", buffering=1)
+
+    def emit(obj):
+        out.write(json.dumps(obj) + "\n")
+        out.flush()
+    return emit
+
+
+EMIT = None   # set by main(): writes one JSON line to the real stdout
 
 
 def parse():
@@ -355,14 +374,16 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
                    "local_moe_ms_per_step": [round(float(v[2]), 3) for v in allv],
                    "a2a_and_dispatch_share": round(max(0.0, 1.0 - max(float(v[2]) for v in allv) / (ms / steps)), 4)}}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        EMIT(line)
     if dist_on:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
 
 def main():
+    global EMIT
     a = parse()
+    EMIT = claim_stdout()
     import torch
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -390,16 +411,16 @@ def main():
             batches = make_batches(T, a.batches, 1000)
             cb = reference_cpu_tier(layer, batches, max(a.cpu_seconds, 5.0), T)
         except FileNotFoundError as exc:
-            print(json.dumps({"impl": "reference", "unavailable": f"reference CPU tier not built: {exc}"}))
+            EMIT({"impl": "reference", "unavailable": f"reference CPU tier not built: {exc}"})
             return
-        print(json.dumps({"metric": METRIC, "value": cb["value"], "unit": "tok/s", "n_gpus": a.gpus, "steps": a.steps,
+        EMIT({"metric": METRIC, "value": cb["value"], "unit": "tok/s", "n_gpus": a.gpus, "steps": a.steps,
                           "warmup": a.warmup, "ms_per_step": round(1e3 * T / cb["value"], 4), "higher_is_better": True,
                           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
                           "data": "synthetic (seeded random EXL3 trellis words; N(0,1) hidden; softmax top-8 routing)",
                           "config": {"workload": f"decode T={T}: one MoE layer E={E} H={H} I={I} top-{TOPK}, uniform "
                                                  f"routing, reference AVX2 CPU tier on host cores"},
                           "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
-                                                      "d2h_bytes_per_step": 0}}))
+                                                      "d2h_bytes_per_step": 0}})
         if dist_on:
             torch.distributed.destroy_process_group()
         return
@@ -581,7 +602,7 @@ def main():
             line["cpu_baseline"] = {"value": None, "unavailable": str(exc)}
 
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        EMIT(line)
     if dist_on:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

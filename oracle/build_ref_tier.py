@@ -8,7 +8,8 @@ extension runs on whatever host CPU the GPU box has:
   tier_v4  -march=x86-64-v4 (adds AVX-512; picked at run time when the host supports it)
 Only this container has the reference tree; the GPU box uses the prebuilt .so files.
 
-usage: python oracle/build_ref_tier.py [--ref /root/reference] [--variants v3,v4]
+usage: python oracle/build_ref_tier.py [--ref REFERENCE_TREE] [--variants v3,v4]
+(REFERENCE_TREE defaults to $DSV41_REFERENCE, else the checkout location of this build container)
 """
 import argparse
 import os
