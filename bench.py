@@ -9,7 +9,7 @@ clamp 10) over one batch: the headline workload is BASELINE configs[1]'s decode 
 with uniform top-8 routing (all 384 experts HBM-resident). Synthetic seeded inputs stand in for real
 weights (no checkpoint): uniform random trellis words, +-1 suh, U(0.5,1.5)/64 svh, N(0,1) bf16
 hidden states, softmax(N(0,1)) top-8 routing. Layers and routing batches are cycled so every step
-streams ~1.7 GB of distinct routed experts' words (inputs far larger than the 126 MB L2).
+streams ~2.7 GB of distinct routed experts' words at N=1 (inputs far larger than the 126 MB L2).
 
 value   = tokens of all ranks / max-over-ranks device time of K steps (inputs resident in HBM)
 e2e     = the same through apply_exl3_fused_moe with pinned host inputs: H2D of x/ids/weights and

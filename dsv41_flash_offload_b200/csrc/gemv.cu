@@ -8,14 +8,15 @@
 //   pass 1 (down):    y = out_block(xt_d . W_d)                -> y    [rows][H] fp16
 //
 // Work unit = (row group of <= 16 rows of one expert, column block, K split). A persistent grid
-// of 2 CTAs per SM walks the units. Per CTA: 16 consumer warps + 1 producer warp.
+// of 2 CTAs per SM walks the units. Per CTA: 8 consumer warps + 1 producer warp.
 //   producer: one 1-D bulk async copy (cp.async.bulk, into this CTA only) per 768/1536-byte trellis
-//             k-row segment and per 256-byte activation row into a 4-stage mbarrier ring;
-//             trellis reads carry an L2 evict-first hint (each expert byte is read once).
-//   consumer warp w: owns one 16-column n-tile; per k-tile it loads the two 32-bit window
-//             words of its lane from the staged tile, decodes its 8 weights into two mma B
-//             fragments in registers, and issues two mma.m16n8k16 (rows = tokens) against the
-//             ldmatrix'd activations. Decoded weights never leave registers.
+//             k-row segment and per 256-byte activation row into a 2-stage mbarrier ring of 16
+//             k-rows per stage; trellis reads carry an L2 evict-first hint (each expert byte is
+//             read once).
+//   consumer warp w: owns two adjacent 16-column n-tiles that share one ldmatrix'd A fragment;
+//             per k-tile and n-tile it loads the window words of its lane from the staged tile,
+//             decodes its 8 weights into two mma B fragments in registers, and issues two
+//             mma.m16n8k16 (rows = tokens). Decoded weights never leave registers.
 // Split-K partials (small batches) are reduced in a fixed order by the last-arriving CTA, so
 // results are deterministic.
 #include "common.cuh"
