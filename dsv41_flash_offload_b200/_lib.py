@@ -19,7 +19,7 @@ OK, E_INVALID, E_CUDA, E_WORKSPACE = 0, -1, -2, -3
 SYMBOLS = (
     "dsv41_last_error", "dsv41_abi_version", "dsv41_build_info", "dsv41_moe_workspace_size",
     "dsv41_moe_forward", "dsv41_moe_forward_noalloc", "dsv41_permute_workspace_size", "dsv41_permute", "dsv41_combine",
-    "dsv41_decode_dense", "dsv41_expert_gemm", "dsv41_expert_gemm_workspace_size", "dsv41_read_status",
+    "dsv41_decode_dense", "dsv41_expert_gemm", "dsv41_expert_gemm_workspace_size", "dsv41_read_status", "dsv41_wait_selftest",
     "dsv41_set_stage_timing", "dsv41_read_stage_times",
 )
 N_STAGES = 7
@@ -84,6 +84,8 @@ def load(path: str | None = None):
         L.dsv41_expert_gemm_workspace_size.argtypes = [i32, i32, i32, i32, C.POINTER(C.c_size_t)]
         L.dsv41_read_status.restype = C.c_int
         L.dsv41_read_status.argtypes = [vp, vp, C.POINTER(C.c_int32)]
+        L.dsv41_wait_selftest.restype = C.c_int
+        L.dsv41_wait_selftest.argtypes = [vp, C.c_uint32, vp]
         L.dsv41_set_stage_timing.restype = C.c_int
         L.dsv41_set_stage_timing.argtypes = [i32]
         L.dsv41_read_stage_times.restype = C.c_int

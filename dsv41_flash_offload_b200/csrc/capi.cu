@@ -584,4 +584,14 @@ int dsv41_read_status(const void* workspace, void* stream, int32_t* status)
     return DSV41_OK;
 }
 
+int dsv41_wait_selftest(void* workspace, uint32_t limit_us, void* stream)
+{
+    if (!workspace) return fail(DSV41_E_INVALID, "NULL workspace");
+    if (limit_us < 1 || limit_us > 2000000u) return fail(DSV41_E_INVALID, "limit_us must be in [1, 2000000]");
+    cudaError_t err = launch_wait_selftest(static_cast<int*>(workspace), (uint64_t)limit_us * 1000ull,
+                                           static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "wait self test launch");
+    return DSV41_OK;
+}
+
 }  // extern "C"

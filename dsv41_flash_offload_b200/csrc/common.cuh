@@ -212,8 +212,9 @@ __device__ __forceinline__ uint64_t globaltimer_ns()
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s, as the reference's combine wait
 
 // Wait for phase `parity` of `bar`. Returns false (and records kStatusWaitTimeout) if it has
-// not completed within kWaitLimitNs or if `abort_flag` is already set.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status)
+// not completed within `limit_ns` (default kWaitLimitNs) or if `abort_flag` is already set.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                                  uint64_t limit_ns = kWaitLimitNs)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
@@ -221,7 +222,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63u) == 0) {
             if (*abort_flag) return false;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (globaltimer_ns() - t0 > limit_ns) {
                 *abort_flag = 1;
                 if (status) atomicExch(status, kStatusWaitTimeout);
                 return false;

@@ -84,6 +84,7 @@ cudaError_t launch_scatter_add(const __half* y, const int* expert_list, int n_li
                                cudaStream_t st);
 
 cudaError_t launch_decode_dense(const void* trellis, int k, int n, __half* w, cudaStream_t st);
+cudaError_t launch_wait_selftest(int* status, uint64_t limit_ns, cudaStream_t st);
 
 int num_sms();
 

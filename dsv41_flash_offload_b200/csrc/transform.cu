@@ -215,4 +215,26 @@ cudaError_t launch_decode_dense(const void* trellis, int k, int n, __half* w, cu
     return cudaGetLastError();
 }
 
+// Failure-detection self test: one warp waits on an mbarrier that nothing ever arrives on, with
+// the same bounded wait the GEMV/GEMM pipelines use. The wait must give up after `limit_ns`,
+// record kStatusWaitTimeout in `status` and return, leaving the context usable.
+__global__ void __launch_bounds__(32) wait_selftest_kernel(int* status, uint64_t limit_ns)
+{
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncwarp();
+    mbar_wait_bounded(&bar, 0, &abort_flag, status, limit_ns);
+}
+
+cudaError_t launch_wait_selftest(int* status, uint64_t limit_ns, cudaStream_t st)
+{
+    wait_selftest_kernel<<<1, 32, 0, st>>>(status, limit_ns);
+    return cudaGetLastError();
+}
+
 }  // namespace dsv41

@@ -255,7 +255,8 @@ def apply_exl3_experts(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: to
 
 def read_status(workspace: torch.Tensor | None = None, device=None) -> int:
     """Synchronise and return (then clear) the device status word of a workspace: 0 = ok,
-    1 = a bounded device-side wait ran out (results of that call are invalid)."""
+    1 = a bounded device-side wait ran out (results of that call are invalid), 3 = more valid routes
+    than max_routes (that call's output is zero)."""
     L = _lib.load()
     if workspace is None:
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -268,6 +269,19 @@ def read_status(workspace: torch.Tensor | None = None, device=None) -> int:
         _lib.check(L.dsv41_read_status(workspace.data_ptr(), _stream_ptr(torch.cuda.current_stream(workspace.device)),
                                        C.byref(st)), "read_status")
     return st.value
+
+
+def wait_selftest(limit_us: int = 20000, device=None) -> int:
+    """Failure-detection self test: one device wait that can never complete runs through the bounded
+    wait of the pipeline kernels with a `limit_us` limit; returns the status word it left (1 when the
+    wait gave up as designed). The context stays usable afterwards."""
+    L = _lib.load()
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    ws = torch.zeros(256, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(L.dsv41_wait_selftest(ws.data_ptr(), int(limit_us), _stream_ptr(torch.cuda.current_stream(dev))),
+                   "wait_selftest")
+    return read_status(ws)
 
 
 # --------------------------------------------------------------------------------------------

@@ -149,6 +149,14 @@ int dsv41_expert_gemm_workspace_size(int32_t total_rows, int32_t n_experts, int3
  * 1 = a bounded device wait ran out, 3 = more valid routes than options.max_routes), then clear it. */
 int dsv41_read_status(const void* workspace, void* stream, int32_t* status);
 
+/* Failure-detection self test (no counterpart entry in the reference; its combine kernel
+ * ct/ft_tier_cu_v.cu:103-127 bounds its device spin the same way, by %globaltimer, and counts a
+ * timeout in a stats word instead of trapping): launches one warp that waits
+ * on a device barrier nothing ever completes, through the bounded wait every pipeline kernel uses;
+ * after limit_us (1..2,000,000) it writes status 1 into the workspace's status word and returns.
+ * Read it with dsv41_read_status; the stream and context stay usable. */
+int dsv41_wait_selftest(void* workspace, uint32_t limit_us, void* stream);
+
 /* Profiling (no counterpart in the reference; used by bench.py to time each kernel on the stream
  * it runs on). While enabled, dsv41_moe_forward records CUDA events at its stage boundaries for up
  * to DSV41_TIMING_MAX_CALLS calls (not under stream capture). dsv41_read_stage_times synchronises

@@ -97,3 +97,17 @@ def test_combine_matches_numpy():
             if pos[t, j] >= 0:
                 ref[t] += float(w[t, j]) * y[pos[t, j]].astype(np.float64)
     np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-5, atol=1e-5)
+
+
+def test_bounded_wait_gives_up_with_status_and_context_survives():
+    """Failure detection without a fault: a device wait that nothing completes must give up after its
+    limit, leave status 1 for the host, and leave the context usable (a decode afterwards is exact)."""
+    import time
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    assert exl3.wait_selftest(limit_us=20000, device=DEV) == 1
+    assert time.perf_counter() - t0 >= 0.02
+    assert exl3.wait_selftest(limit_us=1000, device=DEV) == 1       # status was cleared and set again
+    g = golden("format.npz")
+    W = exl3.decode_dense(torch.from_numpy(g["decode_trellis"]).to(DEV), 64, 128).cpu().numpy()
+    assert np.array_equal(W.view(np.uint16), g["decode_W"].view(np.uint16))

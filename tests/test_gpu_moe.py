@@ -115,6 +115,28 @@ def test_gemm_path_full_shape_vs_oracle(oracle, layer_full):
     assert_close_layer(out.cpu().numpy(), ref, "gemm full shape")
 
 
+@pytest.fixture(scope="module")
+def layer_real():
+    """The model's real expert shape, H 5120 and I 2304 (64 experts to bound memory)."""
+    return exl3.Exl3MoELayer.synthetic(64, 5120, 2304, seed=11, device=DEV)
+
+
+def test_real_shape_top6_vs_oracle(oracle, layer_real):
+    """H 5120 / I 2304 / top-6: a decode batch (GEMV) and four busy experts of 40 rows (GEMM)."""
+    x, ids, w = _inputs(300, 16, 5120, 64, 6)
+    out = exl3.apply_exl3_fused_moe(x, ids, w, layer_real, None, None, LIMIT)
+    assert_close_layer(out.cpu().numpy(), oracle_out(oracle, layer_real, x, ids, w, LIMIT), "real shape decode")
+    T = 40
+    g = torch.Generator().manual_seed(1)
+    experts = torch.tensor([0, 9, 33, 63])
+    ids = torch.stack([experts[torch.randperm(4, generator=g)] for _ in range(T)]).to(DEV)
+    w = torch.softmax(torch.randn(T, 4, generator=g), 1).to(DEV)
+    x = torch.from_numpy(synth.hidden_np(301, T, 5120)).to(DEV, torch.bfloat16)
+    out = exl3.apply_exl3_fused_moe(x, ids, w, layer_real, None, None, LIMIT, fat_threshold=32)
+    assert exl3.read_status(device=DEV) == 0
+    assert_close_layer(out.cpu().numpy(), oracle_out(oracle, layer_real, x, ids, w, LIMIT), "real shape gemm")
+
+
 def test_gemm_matches_gemv_on_prefill(layer_full):
     """Prefill chunk (2048 tokens, Zipf 1.1): tensor-core path for busy experts vs all-GEMV."""
     x, ids, w = _inputs(43, 2048, 4096, 384, kind="zipf", zipf_s=1.1)
