@@ -76,9 +76,13 @@ def parse():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", choices=["decode", "ep40", "prefill-ep"], default="decode",
-                    help="decode: BASELINE configs[1] (default); ep40: configs[3] 40-layer stack, 256-token decode "
-                         "batch; prefill-ep: configs[4] 131,072 tokens x 8 layers, Zipf(1.5)")
+    ap.add_argument("--workload", choices=["decode", "prefill", "ep40", "prefill-ep"], default="decode",
+                    help="decode: BASELINE configs[1] (default); prefill: configs[2] alone (one 16k-token Zipf(1.1) "
+                         "batch, GEMM tensor roofline); ep40: configs[3] 40-layer stack, 256-token decode batch; "
+                         "prefill-ep: configs[4] 131,072 tokens x 8 layers, Zipf(1.5)")
+    ap.add_argument("--prefill-tokens", type=int, default=16384, help="--workload prefill: tokens per batch")
+    ap.add_argument("--experts", type=int, default=E,
+                    help="--workload prefill: experts in the layer (fewer = a smaller case for profiling)")
     return ap.parse_args()
 
 
@@ -141,12 +145,12 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------
 # workload
 # ------------------------------------------------------------------------------------------
-def make_batches(T, n, seed0, kind="uniform", zipf_s=1.1):
+def make_batches(T, n, seed0, kind="uniform", zipf_s=1.1, num_experts=E):
     from dsv41_flash_offload_b200 import synth
     out = []
     for b in range(n):
         x = synth.hidden_np(seed0 + b, T, H)
-        ids, w = synth.routing_np(seed0 + b, T, E, TOPK, kind=kind, zipf_s=zipf_s)
+        ids, w = synth.routing_np(seed0 + b, T, num_experts, TOPK, kind=kind, zipf_s=zipf_s)
         out.append((x, ids, w))
     return out
 
@@ -303,6 +307,75 @@ def reference_cpu_tier(layer, batches, seconds, T):
                       f"{os.path.basename(os.path.dirname(path))} build of kernels/cpu_avx2/ft_tier_ext.cpp"}
 
 
+def prefill_measure(layers, dev, Tp, fat, tf_burst, tf_sus, peak_src, dist_on, n=6, num_experts=E, warm=3):
+    """one Tp-token prefill batch (Zipf(1.1) top-8) through the layers in turn; the
+    tensor roofline covers the two GEMM kernels (busy-expert rows only)."""
+    import numpy as np
+    import torch
+    from dsv41_flash_offload_b200 import exl3
+    hp = make_batches(Tp, 1, 3000, kind="zipf", zipf_s=1.1, num_experts=num_experts)
+    bp = to_device(hp, dev)
+    op = torch.empty(Tp, H, dtype=torch.float32, device=dev)
+
+    def pstep(i):
+        x, ids, w = bp[0]
+        exl3.apply_exl3_fused_moe(x, ids, w, layers[i % len(layers)], None, None, LIMIT, out=op)
+
+    pms = time_steps(pstep, n, warm, dist_on)
+    pst = stage_times(pstep, 4, 1)
+    flops = 2.0 * Tp * TOPK * 3 * H * I
+    cnt = np.bincount(hp[0][1].reshape(-1), minlength=num_experts)
+    busy_rows = int(cnt[cnt > fat].sum()) if fat >= 0 else 0
+    gemm_ms = pst["gemm_gateup"] + pst["gemm_down"]
+    gemm_tf = 2.0 * busy_rows * 3 * H * I / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 and busy_rows else 0.0
+    return {"workload": f"prefill T={Tp}, Zipf(1.1) top-{TOPK} over {num_experts} experts"
+                        + (" (BASELINE configs[2])" if Tp == 16384 and num_experts == E else ""),
+            "tok_s": round(Tp * n / (pms / 1e3), 1), "ms_per_step": round(pms / n, 3),
+            "layer_tflops": round(flops / (pms / n / 1e3) / 1e12, 1),
+            "layer_frac_of_bf16_peak": round(flops / (pms / n / 1e3) / 1e12 / tf_burst, 4),
+            "experts_over_32_rows": int((cnt > 32).sum()), "busy_rows": busy_rows,
+            "max_rows": int(cnt.max()),
+            "path": "decode-GEMV row groups" if fat < 0 else
+                    f"tcgen05 GEMM for experts > {fat} rows, decode-GEMV for the rest",
+            "roofline": {"bound": "tensor", "kernel": "exl3_gemm_kernel<0>+<1> (decode-to-smem tcgen05)",
+                         "achieved": round(gemm_tf, 1), "peak": tf_burst, "unit": "TFLOP/s",
+                         "frac": round(gemm_tf / tf_burst, 4), "peak_sustained": tf_sus,
+                         "peak_source": f"{peak_src} bf16_tflops (cuBLAS bf16 GEMM, burst)"},
+            "stage_ms": {k: round(v, 3) for k, v in pst.items()}}
+
+
+def run_prefill_workload(a, world, rank, dev, dist_on, tf_burst, tf_sus, peak_src):
+    """BASELINE configs[2] on its own (one GPU; other ranks run the same as replicas and only rank 0
+    prints): --prefill-tokens tokens through --layers layers of --experts experts."""
+    import torch
+    from dsv41_flash_offload_b200 import exl3
+    layers = [exl3.Exl3MoELayer.synthetic(a.experts, H, I, seed=0, layer=l, device=dev) for l in range(a.layers)]
+    fat = exl3.FAT_EXPERT_THRESHOLD
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid).replace("GPU-", "")
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid or str(dev.index))
+    pf = prefill_measure(layers, dev, a.prefill_tokens, fat, tf_burst, tf_sus, peak_src, dist_on,
+                         n=max(a.steps, 1), num_experts=a.experts, warm=max(a.warmup, 3))
+    clocks = sampler.stop()
+    line = {"metric": METRIC, "value": round(world * pf["tok_s"], 1), "unit": "tok/s", "n_gpus": world,
+            "steps": max(a.steps, 1), "warmup": max(a.warmup, 3), "ms_per_step": pf["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 (fp16 operands, fp32 accumulate; EXL3 3-bit weights decoded exactly)",
+            "data": "synthetic (seeded random EXL3 trellis words; N(0,1) bf16 hidden; Zipf(1.1) top-8 routing)",
+            "config": {"workload": pf["workload"], "layers_cycled": a.layers,
+                       "parallelism": f"{world} independent replica(s)" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (each step streams every busy expert's words and ~1 GB of rows)"},
+            "roofline": pf["roofline"], "prefill": pf, "clocks": clocks}
+    if rank == 0:
+        EMIT(line)
+    if dist_on:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 # ------------------------------------------------------------------------------------------
 def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst, peak_src):
     """BASELINE configs[3] (ep40) and configs[4] (prefill-ep): a stack of MoE layers, experts sharded
@@ -425,6 +498,8 @@ def main():
             torch.distributed.destroy_process_group()
         return
 
+    if a.workload == "prefill":
+        return run_prefill_workload(a, world, rank, dev, dist_on, tf_burst, tf_sus, peak_src)
     if a.workload != "decode":
         return run_stack_workload(a, a.workload, world, rank, local, dev, dist_on, hbm, tf_burst, peak_src)
 
@@ -563,37 +638,7 @@ def main():
         line["sweep"] = sweep
 
     if not a.no_prefill and world == 1:
-        Tp = 16384
-        hp = make_batches(Tp, 1, 3000, kind="zipf", zipf_s=1.1)
-        bp = to_device(hp, dev)
-        op = torch.empty(Tp, H, dtype=torch.float32, device=dev)
-
-        def pstep(i):
-            x, ids, w = bp[0]
-            exl3.apply_exl3_fused_moe(x, ids, w, layers[i % len(layers)], None, None, LIMIT, out=op)
-
-        n = 6
-        pms = time_steps(pstep, n, 2, dist_on)
-        pst = stage_times(pstep, 4, 1)
-        flops = 2.0 * Tp * TOPK * 3 * H * I
-        import numpy as np
-        cnt = np.bincount(hp[0][1].reshape(-1), minlength=E)
-        busy_rows = int(cnt[cnt > fat].sum()) if fat >= 0 else 0
-        gemm_ms = pst["gemm_gateup"] + pst["gemm_down"]
-        gemm_tf = 2.0 * busy_rows * 3 * H * I / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 and busy_rows else 0.0
-        line["prefill"] = {"workload": f"prefill T={Tp}, Zipf(1.1) top-{TOPK} (BASELINE configs[2])",
-                           "tok_s": round(world * Tp * n / (pms / 1e3), 1), "ms_per_step": round(pms / n, 3),
-                           "layer_tflops": round(flops / (pms / n / 1e3) / 1e12, 1),
-                           "layer_frac_of_bf16_peak": round(flops / (pms / n / 1e3) / 1e12 / tf_burst, 4),
-                           "experts_over_32_rows": int((cnt > 32).sum()), "busy_rows": busy_rows,
-                           "max_rows": int(cnt.max()),
-                           "path": "decode-GEMV row groups" if fat < 0 else
-                                   f"tcgen05 GEMM for experts > {fat} rows, decode-GEMV for the rest",
-                           "roofline": {"bound": "tensor", "kernel": "exl3_gemm_kernel<0>+<1> (decode-to-smem tcgen05)",
-                                        "achieved": round(gemm_tf, 1), "peak": tf_burst, "unit": "TFLOP/s",
-                                        "frac": round(gemm_tf / tf_burst, 4), "peak_sustained": tf_sus,
-                                        "peak_source": f"{peak_src} bf16_tflops (cuBLAS bf16 GEMM, burst)"},
-                           "stage_ms": {k: round(v, 3) for k, v in pst.items()}}
+        line["prefill"] = prefill_measure(layers, dev, 16384, fat, tf_burst, tf_sus, peak_src, dist_on)
 
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         try:

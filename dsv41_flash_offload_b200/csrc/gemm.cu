@@ -7,16 +7,19 @@
 //                     out_block, SwiGLU clamp, fp16, down-input transform -> xt_d
 //   pass 1 (down):    D [rows x 128 features] = xt_d . W_d; epilogue: out_block -> y (fp16)
 // Work unit = (busy expert, row pass of 256 (gate/up) or 512 (down) rows, 128-feature block).
-// One CTA per SM, 10 warps:
-//   warp 0     producer: TMA (cp.async.bulk.tensor, SWIZZLE_128B, into this CTA only) of 128-row x 64-k
-//              activation tiles and 1-D bulk copies of the trellis k-rows, 2-stage mbarrier ring
+// One CTA per SM, 11 warps, three independent mbarrier rings (activations, decoded weights,
+// trellis words):
+//   warp 0     activation producer: TMA (cp.async.bulk.tensor, SWIZZLE_128B, into this CTA only) of
+//              128-row x 64-k tiles; a stage is reused once the MMAs that read it have committed
 //   warp 1     TMEM allocator (512 columns) and single-thread tcgen05.mma issuer
-//              (kind::f16, M=128, N=128, K=16, fp32 accumulators in TMEM); tcgen05.commit frees
-//              a stage and signals the finished accumulators
-//   warps 2-9  decoders: each lane decodes its 8 weights of a 16x16 tile in registers (the same
+//              (kind::f16, M=128, N=128, K=16, fp32 accumulators in TMEM); tcgen05.commit releases
+//              the activation and weight stages and signals the finished accumulators
+//   warp 2     trellis producer: 1-D bulk copies of the compressed k-rows into a 4-8 stage ring
+//              that the decoders release, so the words stream ahead of the MMAs
+//   warps 3-10 decoders: each lane decodes its 8 weights of a 16x16 tile in registers (the same
 //              exact decode as the GEMV) and stores them as K-major 128B-swizzled fp16 B-operand
 //              rows; after the last k chunk they are the epilogue (tcgen05.ld, one row per thread,
-//              128-point Hadamard in registers)
+//              128-point Hadamard in registers, intermediate results parked in TMEM)
 // Experts with more rows than one pass reuse each decoded weight for 256/512 rows.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -27,15 +30,25 @@
 
 namespace dsv41 {
 
-constexpr int kGemmThreads = 320;
+// warp roles
+constexpr int kWarpA = 0;        // TMA producer of the activation tiles
+constexpr int kWarpMma = 1;      // TMEM allocator + single-thread tcgen05.mma issuer
+constexpr int kWarpT = 2;        // bulk-copy producer of the trellis k-rows
+constexpr int kWarpDec0 = 3;     // warps 3..10: decoders, then epilogue
+constexpr int kDecWarps = 8;
+constexpr int kGemmThreads = (kWarpDec0 + kDecWarps) * 32;   // 352
 constexpr int kBM = 128;        // rows per M tile (TMEM lanes)
 constexpr int kBN = 128;        // features per unit (TMEM columns per accumulator)
 constexpr int kBK = 64;         // k per chunk (one 128-byte swizzle row of fp16)
-constexpr int kGStages = 2;
 constexpr int kTileA = kBM * kBK * 2;   // 16 KB
 constexpr int kTileB = kBN * kBK * 2;   // 16 KB
 constexpr int kTrRow = 8 * kTileBytes;  // 768 B: 8 n-tiles of one k-tile row
 
+// Three independent rings per CTA (each with full/empty mbarriers):
+//   A (activations, TMA)   released by tcgen05.commit after the chunk's MMAs
+//   B (decoded weights)    written by the decoders, released by tcgen05.commit
+//   T (trellis k-rows)     filled by the trellis producer, released by the decoders, so the
+//                          compressed words stream ahead of the MMAs by several chunks
 template <int MODE>
 struct GemmCfg {
     static constexpr int nmat = MODE == 0 ? 2 : 1;
@@ -44,8 +57,16 @@ struct GemmCfg {
     static constexpr int a_bytes = nmat * mtiles * kTileA;
     static constexpr int b_bytes = nmat * kTileB;
     static constexpr int t_bytes = nmat * 4 * kTrRow;
-    static constexpr int stage_bytes = a_bytes + b_bytes + t_bytes;   // multiple of 1024
-    static constexpr int smem_bytes = kGStages * stage_bytes + 1024 /* align */ + 256 /* barriers */;
+    static constexpr int a_stages = 2;
+    static constexpr int b_stages = MODE == 0 ? 2 : 3;
+    static constexpr int t_stages = MODE == 0 ? 4 : 8;
+    static constexpr int a_off = 0;
+    static constexpr int b_off = a_off + a_stages * a_bytes;
+    static constexpr int t_off = b_off + b_stages * b_bytes;
+    static constexpr int bar_off = t_off + t_stages * t_bytes;   // multiple of 1024
+    static constexpr int n_bars = 2 * (a_stages + b_stages + t_stages) + 1;
+    static constexpr int smem_bytes = bar_off + 1024 /* align */ + n_bars * 8 + 16;
+    static_assert(smem_bytes <= 232448, "shared memory over the 227 KB per-block limit");
 };
 
 struct GemmParams {
@@ -187,17 +208,20 @@ template <int MODE>
 __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid_constant__ GemmParams p)
 {
     using Cfg = GemmCfg<MODE>;
+    constexpr int AS = Cfg::a_stages, BS = Cfg::b_stages, TS = Cfg::t_stages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
     uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGStages * Cfg::stage_bytes);
-    uint64_t* a_full = bars;                 // [kGStages]
-    uint64_t* t_full = bars + kGStages;      // [kGStages]
-    uint64_t* b_full = bars + 2 * kGStages;  // [kGStages]
-    uint64_t* mma_done = bars + 3 * kGStages;
-    uint64_t* acc_full = bars + 4 * kGStages;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 4 * kGStages + 1);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * kGStages + 2);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::bar_off);
+    uint64_t* a_full = bars;
+    uint64_t* a_empty = a_full + AS;
+    uint64_t* b_full = a_empty + AS;
+    uint64_t* b_empty = b_full + BS;
+    uint64_t* t_full = b_empty + BS;
+    uint64_t* t_empty = t_full + TS;
+    uint64_t* acc_full = t_empty + TS;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + Cfg::n_bars);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::n_bars) + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_fb = p.N / kBN;
@@ -206,17 +230,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
     const int ntile_row = p.N / 16;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kGStages; ++s) {
+        for (int s = 0; s < AS; ++s) {
             mbar_init(&a_full[s], 1);
+            mbar_init(&a_empty[s], 1);
+        }
+        for (int s = 0; s < BS; ++s) {
+            mbar_init(&b_full[s], kDecWarps);
+            mbar_init(&b_empty[s], 1);
+        }
+        for (int s = 0; s < TS; ++s) {
             mbar_init(&t_full[s], 1);
-            mbar_init(&b_full[s], 8);
-            mbar_init(&mma_done[s], 1);
+            mbar_init(&t_empty[s], kDecWarps);
         }
         mbar_init(acc_full, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 1) {
+    if (warp == kWarpMma) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_addr(tmem_slot))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -226,73 +256,84 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    auto stage_a = [&](int s, int mat, int mt) { return smem + s * Cfg::stage_bytes + (mat * Cfg::mtiles + mt) * kTileA; };
-    auto stage_b = [&](int s, int mat) { return smem + s * Cfg::stage_bytes + Cfg::a_bytes + mat * kTileB; };
-    auto stage_t = [&](int s, int mat, int kt) {
-        return smem + s * Cfg::stage_bytes + Cfg::a_bytes + Cfg::b_bytes + (mat * 4 + kt) * kTrRow;
-    };
+    auto stage_a = [&](int s, int mat, int mt) { return smem + Cfg::a_off + s * Cfg::a_bytes + (mat * Cfg::mtiles + mt) * kTileA; };
+    auto stage_b = [&](int s, int mat) { return smem + Cfg::b_off + s * Cfg::b_bytes + mat * kTileB; };
+    auto stage_t = [&](int s, int mat, int kt) { return smem + Cfg::t_off + s * Cfg::t_bytes + (mat * 4 + kt) * kTrRow; };
 
-    if (warp == 0) {
-        // ---------------------------------- producer ----------------------------------
+    if (warp == kWarpA) {
+        // ------------------------------ activation producer ------------------------------
         uint32_t it = 0;
         bool ok = true;
         if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_a)) : "memory");
             if (MODE == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_b)) : "memory");
-        }
-        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-            const int pass = u / n_fb, fb = u % n_fb;
-            const int4 P = p.passes[pass];
-            const int e = P.x, row0 = P.y, rows = P.z;
-            const int act_mt = (rows + kBM - 1) / kBM;
-            const uint8_t* tr[2] = {reinterpret_cast<const uint8_t*>(p.tab_a[e]),
-                                    MODE == 0 ? reinterpret_cast<const uint8_t*>(p.tab_b[e]) : nullptr};
-            for (int c = 0; c < n_chunks; ++c, ++it) {
-                const int s = it % kGStages;
-                const uint32_t round = it / kGStages;
-                if (!mbar_wait_bounded(&mma_done[s], (round & 1) ^ 1, abort_flag, p.status)) {
-                    ok = false;
-                    break;
-                }
-                if (lane == 0) {
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                const int4 P = p.passes[u / n_fb];
+                const int row0 = P.y, act_mt = (P.z + kBM - 1) / kBM;
+                for (int c = 0; c < n_chunks; ++c, ++it) {
+                    const int s = it % AS;
+                    if (!mbar_wait_bounded(&a_empty[s], ((it / AS) & 1) ^ 1, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
                     mbar_arrive_expect_tx(&a_full[s], Cfg::nmat * act_mt * kTileA);
                     for (int mat = 0; mat < Cfg::nmat; ++mat)
                         for (int mt = 0; mt < act_mt; ++mt)
                             tma_load_2d(stage_a(s, mat, mt), mat ? &p.tm_b : &p.tm_a, c * kBK, row0 + mt * kBM, &a_full[s]);
-                    mbar_arrive_expect_tx(&t_full[s], Cfg::t_bytes);
                 }
+            }
+            // on abort, let the copies already issued land before the CTA exits
+            for (uint32_t q = 1; !ok && q <= (it < (uint32_t)AS ? it : (uint32_t)AS); ++q) {
+                const uint32_t j = it - q;
+                const uint64_t t0 = globaltimer_ns();
+                while (!mbar_try_wait(&a_full[j % AS], (j / AS) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {}
+            }
+        }
+        __syncwarp();
+    } else if (warp == kWarpT) {
+        // ------------------------------ trellis producer ------------------------------
+        uint32_t it = 0;
+        bool ok = true;
+        const uint64_t pol = l2_policy_evict_first();
+        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+            const int pass = u / n_fb, fb = u % n_fb;
+            const int e = p.passes[pass].x;
+            const uint8_t* tr[2] = {reinterpret_cast<const uint8_t*>(p.tab_a[e]),
+                                    MODE == 0 ? reinterpret_cast<const uint8_t*>(p.tab_b[e]) : nullptr};
+            for (int c = 0; c < n_chunks; ++c, ++it) {
+                const int s = it % TS;
+                if (!mbar_wait_bounded(&t_empty[s], ((it / TS) & 1) ^ 1, abort_flag, p.status)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) mbar_arrive_expect_tx(&t_full[s], Cfg::t_bytes);
                 __syncwarp();
                 if (lane < Cfg::nmat * 4) {
                     const int mat = lane / 4, kt = lane % 4;
                     const uint8_t* src = tr[mat] + ((size_t)(c * 4 + kt) * ntile_row + fb * 8) * kTileBytes;
-                    bulk_g2s(stage_t(s, mat, kt), src, kTrRow, &t_full[s], l2_policy_evict_first());
+                    bulk_g2s(stage_t(s, mat, kt), src, kTrRow, &t_full[s], pol);
                 }
             }
         }
         if (!ok && lane == 0) {
-            const uint32_t n_back = it < (uint32_t)kGStages ? it : (uint32_t)kGStages;
-            for (uint32_t q = 1; q <= n_back; ++q) {
+            for (uint32_t q = 1; q <= (it < (uint32_t)TS ? it : (uint32_t)TS); ++q) {
                 const uint32_t j = it - q;
                 const uint64_t t0 = globaltimer_ns();
-                while (!(mbar_try_wait(&a_full[j % kGStages], (j / kGStages) & 1) &&
-                         mbar_try_wait(&t_full[j % kGStages], (j / kGStages) & 1)) &&
-                       globaltimer_ns() - t0 < kWaitLimitNs) {}
+                while (!mbar_try_wait(&t_full[j % TS], (j / TS) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {}
             }
         }
-    } else if (warp == 1) {
+        __syncwarp();
+    } else if (warp == kWarpMma) {
         // ---------------------------------- MMA issuer ----------------------------------
         if (lane == 0) {
-            uint32_t it = 0, units_done = 0;
+            uint32_t ia = 0, ib = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++units_done) {
-                const int pass = u / n_fb;
-                const int rows = p.passes[pass].z;
-                const int act_mt = (rows + kBM - 1) / kBM;
-                for (int c = 0; c < n_chunks; ++c, ++it) {
-                    const int s = it % kGStages;
-                    const uint32_t round = it / kGStages;
-                    if (!mbar_wait_bounded(&a_full[s], round & 1, abort_flag, p.status) ||
-                        !mbar_wait_bounded(&b_full[s], round & 1, abort_flag, p.status)) {
+            for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+                const int act_mt = (p.passes[u / n_fb].z + kBM - 1) / kBM;
+                for (int c = 0; c < n_chunks; ++c, ++ia, ++ib) {
+                    const int sa = ia % AS, sb = ib % BS;
+                    if (!mbar_wait_bounded(&b_full[sb], (ib / BS) & 1, abort_flag, p.status) ||
+                        !mbar_wait_bounded(&a_full[sa], (ia / AS) & 1, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
@@ -300,26 +341,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                     for (int mt = 0; mt < act_mt; ++mt)
                         for (int mat = 0; mat < Cfg::nmat; ++mat) {
                             const uint32_t d = tmem + (uint32_t)((mt * Cfg::nmat + mat) * kBN);
-                            const uint32_t a0 = smem_addr(stage_a(s, mat, mt)), b0 = smem_addr(stage_b(s, mat));
+                            const uint32_t a0 = smem_addr(stage_a(sa, mat, mt)), b0 = smem_addr(stage_b(sb, mat));
 #pragma unroll
                             for (int kk = 0; kk < kBK / 16; ++kk)
                                 umma_f16(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), (c > 0 || kk > 0) ? 1u : 0u);
                         }
-                    umma_commit(&mma_done[s]);
+                    umma_commit(&a_empty[sa]);
+                    umma_commit(&b_empty[sb]);
                 }
                 if (ok) umma_commit(acc_full);
             }
-            // wait for the last MMAs before TMEM is released
-            if (it > 0) {
-                const uint32_t j = it - 1;
+            // the last MMAs must finish before TMEM is released
+            if (ib > 0) {
+                const uint32_t j = ib - 1;
                 const uint64_t t0 = globaltimer_ns();
-                while (!mbar_try_wait(&mma_done[j % kGStages], (j / kGStages) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {}
+                while (!mbar_try_wait(&b_empty[j % BS], (j / BS) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {}
             }
         }
         __syncwarp();
     } else {
         // ------------------------------- decoders + epilogue -------------------------------
-        const int d = warp - 2;                       // 0..7
+        const int d = warp - kWarpDec0;               // 0..7
         const LaneWindow lw = lane_window_setup(lane);
         const uint32_t k16 = p.k16;
         const int r0 = (lane & 3) * 2, c0 = lane >> 2;
@@ -328,42 +370,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
         const int dmat = MODE == 0 ? d / 4 : 0;
         const int dkt = MODE == 0 ? d % 4 : d / 2;
         const int nt0 = MODE == 0 ? 0 : 4 * (d % 2);
-        const int ntn = MODE == 0 ? 8 : 4;
+        constexpr int ntn = MODE == 0 ? 8 : 4;
+        // byte offsets of this lane's four B words inside one 16-column n-tile of the swizzled
+        // K-major operand: element (n, k) at (n/8)*1024 + (n%8)*128 + ((k/8) ^ (n%8))*16 + (k%8)*2
+        uint32_t boff[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int n = c0 + ((q >> 1) << 3);
+            const int k = dkt * 16 + r0 + ((q & 1) << 3);
+            boff[q] = (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + (((k >> 3) ^ (n & 7)) * 16) + (k & 7) * 2);
+        }
         const int quarter = warp & 3;                 // TMEM lanes this warp may access
-        uint32_t it = 0, units_done = 0;
+        uint32_t it = 0, ib = 0, units_done = 0;
         bool ok = true;
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++units_done) {
             const int pass = u / n_fb, fb = u % n_fb;
             const int4 P = p.passes[pass];
             const int e = P.x, row0 = P.y, rows = P.z;
-            for (int c = 0; c < n_chunks; ++c, ++it) {
-                const int s = it % kGStages;
-                const uint32_t round = it / kGStages;
-                if (!mbar_wait_bounded(&t_full[s], round & 1, abort_flag, p.status)) {
+            for (int c = 0; c < n_chunks; ++c, ++it, ++ib) {
+                const int st = it % TS, sb = ib % BS;
+                if (!mbar_wait_bounded(&t_full[st], (it / TS) & 1, abort_flag, p.status) ||
+                    !mbar_wait_bounded(&b_empty[sb], ((ib / BS) & 1) ^ 1, abort_flag, p.status)) {
                     ok = false;
                     break;
                 }
-                const uint32_t* trw = reinterpret_cast<const uint32_t*>(stage_t(s, dmat, dkt));
-                uint8_t* bt = stage_b(s, dmat);
-#pragma unroll 2
+                const uint32_t* trw = reinterpret_cast<const uint32_t*>(stage_t(st, dmat, dkt));
+                uint8_t* bt = stage_b(sb, dmat) + nt0 * 2048;
+#pragma unroll 4
                 for (int j = 0; j < ntn; ++j) {
-                    const int nt = nt0 + j;
-                    const uint32_t* tw = trw + nt * kTileWords;
+                    const uint32_t* tw = trw + (nt0 + j) * kTileWords;
                     uint32_t b[4];
                     decode_lane_u(tw[lw.q0], tw[lw.q1], tw[lw.q2], lw.r8, k16, b);
-                    // B operand row n (feature), K-major 128B-swizzled: element (n, k) at
-                    // (n/8)*1024 + (n%8)*128 + ((2k/16) ^ (n%8))*16 + (2k)%16
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int n = nt * 16 + c0 + ((q >> 1) << 3);
-                        const int k = dkt * 16 + r0 + ((q & 1) << 3);
-                        const int chunk = (k >> 3) ^ (n & 7);
-                        *reinterpret_cast<uint32_t*>(bt + (n >> 3) * 1024 + (n & 7) * 128 + chunk * 16 + (k & 7) * 2) = b[q];
-                    }
+                    for (int q = 0; q < 4; ++q) *reinterpret_cast<uint32_t*>(bt + j * 2048 + boff[q]) = b[q];
                 }
                 fence_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&b_full[s]);
+                if (lane == 0) {
+                    mbar_arrive(&b_full[sb]);
+                    mbar_arrive(&t_empty[st]);
+                }
             }
             if (!ok) break;
             // ------------------------------- epilogue -------------------------------
@@ -382,44 +428,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 if (MODE == 0) {
                     const uint32_t colg = (uint32_t)((mt * 2 + 0) * kBN), colu = (uint32_t)((mt * 2 + 1) * kBN);
                     const __half* svg = p.svh_a + (size_t)e * 2 * p.N + fb * kBN;
+                    // out_block of gate and of up, each written back to its TMEM columns
+#pragma unroll 1
+                    for (int m = 0; m < 2; ++m) {
+                        const uint32_t col = m ? colu : colg;
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            float t[32];
+                            tmem_ld32(lane_addr + col + q * 32, t);
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) v[q * 32 + i] = t[i];
+                        }
+                        out_block128(v, svg + m * p.N);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            float t[32];
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) t[i] = v[q * 32 + i];
+                            tmem_st32(lane_addr + col + q * 32, t);
+                        }
+                    }
+                    // SwiGLU and the down-input scale, 32 columns at a time (into the gate columns)
+                    const __half* sd = p.suh_d + (size_t)e * p.N + fb * kBN;
+#pragma unroll 1
+                    for (int q = 0; q < 4; ++q) {
+                        float g[32], uu[32];
+                        tmem_ld32(lane_addr + colg + q * 32, g);
+                        tmem_ld32(lane_addr + colu + q * 32, uu);
+#pragma unroll
+                        for (int c8 = 0; c8 < 4; ++c8) {
+                            float s8[8];
+                            load_half8(sd + q * 32 + c8 * 8, s8);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i)
+                                g[c8 * 8 + i] = __fmul_rn(r16(act_gu(g[c8 * 8 + i], uu[c8 * 8 + i], p.limit)), s8[i]);
+                        }
+                        tmem_st32(lane_addr + colg + q * 32, g);
+                    }
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         float t[32];
                         tmem_ld32(lane_addr + colg + q * 32, t);
 #pragma unroll
                         for (int i = 0; i < 32; ++i) v[q * 32 + i] = t[i];
-                    }
-                    out_block128(v, svg);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        float t[32];
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) t[i] = v[q * 32 + i];
-                        tmem_st32(lane_addr + colg + q * 32, t);
-                    }
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        float t[32];
-                        tmem_ld32(lane_addr + colu + q * 32, t);
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[q * 32 + i] = t[i];
-                    }
-                    out_block128(v, svg + p.N);
-                    const __half* sd = p.suh_d + (size_t)e * p.N + fb * kBN;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        float g[32];
-                        tmem_ld32(lane_addr + colg + q * 32, g);
-#pragma unroll
-                        for (int c8 = 0; c8 < 4; ++c8) {
-                            float s8[8];
-                            load_half8(sd + q * 32 + c8 * 8, s8);
-#pragma unroll
-                            for (int i = 0; i < 8; ++i) {
-                                const int idx = q * 32 + c8 * 8 + i;
-                                v[idx] = __fmul_rn(r16(act_gu(g[c8 * 8 + i], v[idx], p.limit)), s8[i]);
-                            }
-                        }
                     }
                     had128_thread(v);
 #pragma unroll
@@ -452,7 +503,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
         }
     }
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kWarpMma) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
     }
