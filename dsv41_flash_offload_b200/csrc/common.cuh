@@ -240,6 +240,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
         : "memory");
 }
+// bring `bytes` (multiple of 16, 16-byte aligned) of global memory into L2, no completion tracking
+__device__ __forceinline__ void l2_prefetch_bulk(const void* src, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ uint64_t l2_policy_evict_first()
 {
     uint64_t p;

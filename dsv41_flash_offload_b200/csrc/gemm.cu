@@ -7,7 +7,7 @@
 //                     out_block, SwiGLU clamp, fp16, down-input transform -> xt_d
 //   pass 1 (down):    D [rows x 128 features] = xt_d . W_d; epilogue: out_block -> y (fp16)
 // Work unit = (busy expert, row pass of 256 (gate/up) or 512 (down) rows, 128-feature block).
-// One CTA per SM, 11 warps, three independent mbarrier rings (activations, decoded weights,
+// One CTA per SM, 12 warps, three independent mbarrier rings (activations, decoded weights,
 // trellis words):
 //   warp 0     activation producer: TMA (cp.async.bulk.tensor, SWIZZLE_128B, into this CTA only) of
 //              128-row x 64-k tiles; a stage is reused once the MMAs that read it have committed
@@ -16,7 +16,7 @@
 //              the activation and weight stages and signals the finished accumulators
 //   warp 2     trellis producer: 1-D bulk copies of the compressed k-rows into a 4-8 stage ring
 //              that the decoders release, so the words stream ahead of the MMAs
-//   warps 3-10 decoders: each lane decodes its 8 weights of a 16x16 tile in registers (the same
+//   warps 4-11 decoders: each lane decodes its 8 weights of a 16x16 tile in registers (the same
 //              exact decode as the GEMV) and stores them as K-major 128B-swizzled fp16 B-operand
 //              rows; after the last k chunk they are the epilogue (tcgen05.ld, one row per thread,
 //              128-point Hadamard in registers, intermediate results parked in TMEM)
@@ -31,17 +31,35 @@
 namespace dsv41 {
 
 // warp roles
+// (warp w issues on SM sub-partition w % 4 and may only touch TMEM lanes 32*(w%4)..+31: the three
+// producer/issuer warps and the idle warp 3 take one sub-partition each, so every sub-partition
+// runs one of them plus two decoders, and the decoders cover each TMEM lane quarter twice)
 constexpr int kWarpA = 0;        // TMA producer of the activation tiles
 constexpr int kWarpMma = 1;      // TMEM allocator + single-thread tcgen05.mma issuer
 constexpr int kWarpT = 2;        // bulk-copy producer of the trellis k-rows
-constexpr int kWarpDec0 = 3;     // warps 3..10: decoders, then epilogue
+constexpr int kWarpDec0 = 4;     // warps 4..11: decoders, then epilogue (warp 3 idles)
 constexpr int kDecWarps = 8;
-constexpr int kGemmThreads = (kWarpDec0 + kDecWarps) * 32;   // 352
+constexpr int kGemmThreads = (kWarpDec0 + kDecWarps) * 32;   // 384
+#ifndef DSV41_GEMM_DEC_UNROLL
+#define DSV41_GEMM_DEC_UNROLL 4
+#endif
+constexpr int kDecUnroll = DSV41_GEMM_DEC_UNROLL;   // tiles of the decode loop in flight per warp
 constexpr int kBM = 128;        // rows per M tile (TMEM lanes)
 constexpr int kBN = 128;        // features per unit (TMEM columns per accumulator)
-constexpr int kBK = 64;         // k per chunk (one 128-byte swizzle row of fp16)
-constexpr int kTileA = kBM * kBK * 2;   // 16 KB
-constexpr int kTileB = kBN * kBK * 2;   // 16 KB
+#ifndef DSV41_GEMM_BK
+#define DSV41_GEMM_BK 64
+#endif
+// k per chunk: 64 (one 128-byte SWIZZLE_128B row of fp16 per operand row) or 32 (SWIZZLE_64B, twice
+// the ring stages in the same shared memory). Measured on B200, 16k-token prefill: gate/up GEMM
+// 7.36 ms with 64, 8.68 ms with 32 (twice the barrier hand-offs per FLOP; the decoders, not the
+// ring depth, bound the main loop).
+constexpr int kBK = DSV41_GEMM_BK;
+static_assert(kBK == 32 || kBK == 64, "chunk must be 32 or 64");
+constexpr int kKT = kBK / 16;           // k-tiles (16 k) per chunk
+constexpr int kRowB = kBK * 2;          // bytes of one operand row in a stage (= swizzle span)
+constexpr int kAtom = 8 * kRowB;        // bytes of one 8-row swizzle atom
+constexpr int kTileA = kBM * kRowB;     // one 128-row activation tile
+constexpr int kTileB = kBN * kRowB;     // one 128-feature decoded weight tile
 constexpr int kTrRow = 8 * kTileBytes;  // 768 B: 8 n-tiles of one k-tile row
 
 // Three independent rings per CTA (each with full/empty mbarriers):
@@ -56,10 +74,10 @@ struct GemmCfg {
     static constexpr int rows_per_pass = mtiles * kBM;
     static constexpr int a_bytes = nmat * mtiles * kTileA;
     static constexpr int b_bytes = nmat * kTileB;
-    static constexpr int t_bytes = nmat * 4 * kTrRow;
-    static constexpr int a_stages = 2;
-    static constexpr int b_stages = MODE == 0 ? 2 : 3;
-    static constexpr int t_stages = MODE == 0 ? 4 : 8;
+    static constexpr int t_bytes = nmat * kKT * kTrRow;
+    static constexpr int a_stages = 2 * (64 / kBK);
+    static constexpr int b_stages = (MODE == 0 ? 2 : 3) * (64 / kBK);
+    static constexpr int t_stages = (MODE == 0 ? 4 : 8) * (64 / kBK);
     static constexpr int a_off = 0;
     static constexpr int b_off = a_off + a_stages * a_bytes;
     static constexpr int t_off = b_off + b_stages * b_bytes;
@@ -88,11 +106,13 @@ struct GemmParams {
 // ---------------------------------------------------------------------------------------------
 // tcgen05 / TMA primitives
 // ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
+__device__ __forceinline__ uint64_t sw_desc(uint32_t saddr)
 {
-    // K-major, SWIZZLE_128B canonical layout: 8-row atoms of 128 B rows, atoms 1024 B apart
-    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+    // K-major swizzled canonical layout: 8-row atoms of kRowB-byte rows, atoms kAtom bytes apart;
+    // layout type 2 = SWIZZLE_128B, 4 = SWIZZLE_64B (tcgen05 shared memory descriptor, version 1)
+    constexpr uint64_t layout = kBK == 64 ? 2 : 4;
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(kAtom >> 4) << 32) |
+           ((uint64_t)1 << 46) | (layout << 61);
 }
 
 // kind::f16, fp16 A/B, fp32 D, K-major A and B, N = 128, M = 128
@@ -258,7 +278,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
 
     auto stage_a = [&](int s, int mat, int mt) { return smem + Cfg::a_off + s * Cfg::a_bytes + (mat * Cfg::mtiles + mt) * kTileA; };
     auto stage_b = [&](int s, int mat) { return smem + Cfg::b_off + s * Cfg::b_bytes + mat * kTileB; };
-    auto stage_t = [&](int s, int mat, int kt) { return smem + Cfg::t_off + s * Cfg::t_bytes + (mat * 4 + kt) * kTrRow; };
+    auto stage_t = [&](int s, int mat, int kt) { return smem + Cfg::t_off + s * Cfg::t_bytes + (mat * kKT + kt) * kTrRow; };
 
     if (warp == kWarpA) {
         // ------------------------------ activation producer ------------------------------
@@ -295,6 +315,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
         uint32_t it = 0;
         bool ok = true;
         const uint64_t pol = l2_policy_evict_first();
+        // this lane's k-row segment of chunk c of unit u (lanes < nmat*4; others return null)
+        auto src_of = [&](int u, int c) -> const uint8_t* {
+            if (lane >= Cfg::nmat * kKT || u >= n_units) return nullptr;
+            const int e = p.passes[u / n_fb].x, fb = u % n_fb;
+            const int64_t base = (lane / kKT) ? p.tab_b[e] : p.tab_a[e];
+            return reinterpret_cast<const uint8_t*>(base) + ((size_t)(c * kKT + lane % kKT) * ntile_row + fb * 8) * kTileBytes;
+        };
+        // L2 prefetch runs kTrPrefetch chunks ahead of the copies (into the next unit near the end),
+        // so the ring's copies see L2 latency rather than HBM latency
+        constexpr int kTrPrefetch = 16 * (64 / kBK);
+        for (int c = 0; c < kTrPrefetch && c < n_chunks; ++c)
+            if (const uint8_t* q = src_of(blockIdx.x, c)) l2_prefetch_bulk(q, kTrRow);
         for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
             const int pass = u / n_fb, fb = u % n_fb;
             const int e = p.passes[pass].x;
@@ -302,15 +334,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                                     MODE == 0 ? reinterpret_cast<const uint8_t*>(p.tab_b[e]) : nullptr};
             for (int c = 0; c < n_chunks; ++c, ++it) {
                 const int s = it % TS;
+                {
+                    const int cp = c + kTrPrefetch;
+                    const uint8_t* q = cp < n_chunks ? src_of(u, cp) : src_of(u + gridDim.x, cp - n_chunks);
+                    if (q && cp - n_chunks < n_chunks) l2_prefetch_bulk(q, kTrRow);
+                }
                 if (!mbar_wait_bounded(&t_empty[s], ((it / TS) & 1) ^ 1, abort_flag, p.status)) {
                     ok = false;
                     break;
                 }
                 if (lane == 0) mbar_arrive_expect_tx(&t_full[s], Cfg::t_bytes);
                 __syncwarp();
-                if (lane < Cfg::nmat * 4) {
-                    const int mat = lane / 4, kt = lane % 4;
-                    const uint8_t* src = tr[mat] + ((size_t)(c * 4 + kt) * ntile_row + fb * 8) * kTileBytes;
+                if (lane < Cfg::nmat * kKT) {
+                    const int mat = lane / kKT, kt = lane % kKT;
+                    const uint8_t* src = tr[mat] + ((size_t)(c * kKT + kt) * ntile_row + fb * 8) * kTileBytes;
                     bulk_g2s(stage_t(s, mat, kt), src, kTrRow, &t_full[s], pol);
                 }
             }
@@ -328,6 +365,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
         if (lane == 0) {
             uint32_t ia = 0, ib = 0;
             bool ok = true;
+            // One thread issues every MMA, so its per-MMA instruction count bounds the tensor
+            // pipe: the descriptors of stage 0 are built once, and a stage / tile / k step only
+            // adds its byte offset / 16 to the 14-bit start-address field (shared memory stays
+            // below 256 KB, so the field never carries).
+            const uint64_t adesc0 = sw_desc(smem_addr(smem + Cfg::a_off));
+            const uint64_t bdesc0 = sw_desc(smem_addr(smem + Cfg::b_off));
             for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
                 const int act_mt = (p.passes[u / n_fb].z + kBM - 1) / kBM;
                 for (int c = 0; c < n_chunks; ++c, ++ia, ++ib) {
@@ -338,14 +381,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                         break;
                     }
                     tc_fence_after();
-                    for (int mt = 0; mt < act_mt; ++mt)
+                    const uint64_t ad_s = adesc0 + (uint64_t)((sa * Cfg::a_bytes) >> 4);
+                    const uint64_t bd_s = bdesc0 + (uint64_t)((sb * Cfg::b_bytes) >> 4);
+                    const uint32_t acc0 = c > 0 ? 1u : 0u;
+#pragma unroll
+                    for (int mt = 0; mt < Cfg::mtiles; ++mt) {
+                        if (mt >= act_mt) break;
+#pragma unroll
                         for (int mat = 0; mat < Cfg::nmat; ++mat) {
                             const uint32_t d = tmem + (uint32_t)((mt * Cfg::nmat + mat) * kBN);
-                            const uint32_t a0 = smem_addr(stage_a(sa, mat, mt)), b0 = smem_addr(stage_b(sb, mat));
+                            const uint64_t ad = ad_s + (uint64_t)(((mat * Cfg::mtiles + mt) * kTileA) >> 4);
+                            const uint64_t bd = bd_s + (uint64_t)((mat * kTileB) >> 4);
 #pragma unroll
                             for (int kk = 0; kk < kBK / 16; ++kk)
-                                umma_f16(d, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), (c > 0 || kk > 0) ? 1u : 0u);
+                                umma_f16(d, ad + 2 * kk, bd + 2 * kk, kk ? 1u : acc0);
                         }
+                    }
                     umma_commit(&a_empty[sa]);
                     umma_commit(&b_empty[sb]);
                 }
@@ -359,26 +410,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp >= kWarpDec0) {
         // ------------------------------- decoders + epilogue -------------------------------
         const int d = warp - kWarpDec0;               // 0..7
         const LaneWindow lw = lane_window_setup(lane);
         const uint32_t k16 = p.k16;
         const int r0 = (lane & 3) * 2, c0 = lane >> 2;
-        // decode assignment: gate/up: warp d -> matrix d/4, k-tile d%4, n-tiles 0..7
-        //                    down:    warp d -> k-tile d/2, n-tiles 4*(d%2) .. +3
-        const int dmat = MODE == 0 ? d / 4 : 0;
-        const int dkt = MODE == 0 ? d % 4 : d / 2;
-        const int nt0 = MODE == 0 ? 0 : 4 * (d % 2);
-        constexpr int ntn = MODE == 0 ? 8 : 4;
+        // decode assignment: the chunk's nmat * kKT (matrix, k-tile) rows of 8 n-tiles are split
+        // evenly over the 8 decoder warps (wpg warps per row, ntn adjacent n-tiles each)
+        constexpr int wpg = kDecWarps / (Cfg::nmat * kKT);
+        constexpr int ntn = 8 / wpg;
+        const int grp = d / wpg;
+        const int dmat = grp / kKT, dkt = grp % kKT;
+        const int nt0 = (d % wpg) * ntn;
         // byte offsets of this lane's four B words inside one 16-column n-tile of the swizzled
-        // K-major operand: element (n, k) at (n/8)*1024 + (n%8)*128 + ((k/8) ^ (n%8))*16 + (k%8)*2
+        // K-major operand: element (n, k) at (n/8)*kAtom + (n%8)*kRowB + ((k/8) ^ sw(n%8))*16 + (k%8)*2,
+        // sw(r) = r for the 128-byte swizzle and r/2 for the 64-byte one
         uint32_t boff[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const int n = c0 + ((q >> 1) << 3);
             const int k = dkt * 16 + r0 + ((q & 1) << 3);
-            boff[q] = (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + (((k >> 3) ^ (n & 7)) * 16) + (k & 7) * 2);
+            const int sw = kBK == 64 ? (n & 7) : ((n & 7) >> 1);
+            boff[q] = (uint32_t)((n >> 3) * kAtom + (n & 7) * kRowB + (((k >> 3) ^ sw) * 16) + (k & 7) * 2);
         }
         const int quarter = warp & 3;                 // TMEM lanes this warp may access
         uint32_t it = 0, ib = 0, units_done = 0;
@@ -395,14 +449,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                     break;
                 }
                 const uint32_t* trw = reinterpret_cast<const uint32_t*>(stage_t(st, dmat, dkt));
-                uint8_t* bt = stage_b(sb, dmat) + nt0 * 2048;
-#pragma unroll 4
+                uint8_t* bt = stage_b(sb, dmat) + nt0 * 2 * kAtom;
+#pragma unroll kDecUnroll
                 for (int j = 0; j < ntn; ++j) {
                     const uint32_t* tw = trw + (nt0 + j) * kTileWords;
                     uint32_t b[4];
                     decode_lane_u(tw[lw.q0], tw[lw.q1], tw[lw.q2], lw.r8, k16, b);
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) *reinterpret_cast<uint32_t*>(bt + j * 2048 + boff[q]) = b[q];
+                    for (int q = 0; q < 4; ++q) *reinterpret_cast<uint32_t*>(bt + j * 2 * kAtom + boff[q]) = b[q];
                 }
                 fence_async_smem();
                 __syncwarp();
@@ -550,7 +604,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     return fn;
 }
 
-// [rows][K] fp16 rows, box 64 (k) x 128 (rows), 128-byte swizzle, zero fill out of bounds
+// [rows][K] fp16 rows, box kBK (k) x 128 (rows), swizzle matching the descriptors, zero fill out of bounds
 static cudaError_t make_map(CUtensorMap* m, const void* base, int rows, int K)
 {
     auto fn = encode_fn();
@@ -558,9 +612,10 @@ static cudaError_t make_map(CUtensorMap* m, const void* base, int rows, int K)
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)(rows > 0 ? rows : 1)};
     const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
     const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+    const CUtensorMapSwizzle swz = kBK == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
