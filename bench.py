@@ -80,6 +80,9 @@ def parse():
                     help="decode: BASELINE configs[1] (default); prefill: configs[2] alone (one 16k-token Zipf(1.1) "
                          "batch, GEMM tensor roofline); ep40: configs[3] 40-layer stack, 256-token decode batch; "
                          "prefill-ep: configs[4] 131,072 tokens x 8 layers, Zipf(1.5)")
+    ap.add_argument("--ep", choices=["peer", "nccl"], default="peer",
+                    help="N > 1 decode exchange: peer = token rows and expert outputs read from peers' memory inside "
+                         "the row transform and combine kernels (EPPeerMoE); nccl = fixed-slot all-to-all (EPMoE)")
     ap.add_argument("--prefill-tokens", type=int, default=16384, help="--workload prefill: tokens per batch")
     ap.add_argument("--experts", type=int, default=E,
                     help="--workload prefill: experts in the layer (fewer = a smaller case for profiling)")
@@ -241,13 +244,15 @@ def layer_bytes(ids, T):
     return d * EXPERT_BYTES + T * H * 2 + T * H * 4 + T * TOPK * 12
 
 
-def traffic_from_profile():
-    """dram bytes per launch of the gate/up GEMV from the committed ncu summary, if present."""
+def traffic_ratio_from_profile():
+    """DRAM bytes / algorithmic bytes of the gate/up GEMV launch captured with ncu (committed summary),
+    or None. Traffic per launch of this run = ratio x its algorithmic bytes per launch (the capture is
+    the same kernel and shape; the bytes scale with the distinct experts a batch routes to)."""
     p = os.path.join(ROOT, "profiles", "gemv_gateup_decode_T64.txt")
     if not os.path.exists(p):
         return None
     for line in open(p):
-        if line.startswith("traffic_bytes_per_launch:"):
+        if line.startswith("traffic_over_algorithmic:"):
             try:
                 return float(line.split(":")[1].split()[0])
             except ValueError:
@@ -385,7 +390,7 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
     import numpy as np
     import torch
     from dsv41_flash_offload_b200 import exl3, synth
-    from dsv41_flash_offload_b200.ep import EPMoE, local_layer_fn
+    from dsv41_flash_offload_b200.ep import EPMoE, EPPeerMoE, local_layer_fn
 
     n_layers, total, zipf = (40, 256, None) if kind == "ep40" else (8, 131072, 1.5)
     T = total // world
@@ -393,7 +398,10 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
     lo, hi = rank * e_loc, (rank + 1) * e_loc
     layers = [exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, layer=l, device=dev,
                                           expert_range=(lo, hi) if world > 1 else None) for l in range(n_layers)]
-    eps = [EPMoE(local_layer_fn(lay, LIMIT), E) for lay in layers]
+    # decode stack: peer-memory exchange (one set of shared buffers for all layers); prefill: NCCL
+    # all-to-all with compact (deduplicated) dispatch
+    peer = EPPeerMoE(layers[0], E, T, TOPK, limit=LIMIT) if kind == "ep40" and world > 1 and a.ep == "peer" else None
+    eps = [] if peer is not None else [EPMoE(local_layer_fn(lay, LIMIT), E) for lay in layers]
     if kind == "ep40":
         for ep in eps:
             ep.slot_capacity = T  # decode batches: fixed-slot dispatch, no host synchronisation
@@ -409,15 +417,18 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
         x = x0
         for l in range(n_layers):
             ids, w = routes[l]
-            x = (x.float() + eps[l](x, ids, w)).to(torch.bfloat16)
+            y = peer(x, ids, w, layer=layers[l]) if peer is not None else eps[l](x, ids, w)
+            x = (x.float() + y).to(torch.bfloat16)
         return x
 
-    steps, warm = (max(1, min(a.steps, 10)), max(1, min(a.warmup, 2))) if kind == "ep40" else (max(1, min(a.steps, 3)), 1)
+    steps, warm = (max(1, min(a.steps, 10)) if kind == "ep40" else max(1, min(a.steps, 3))), 3
     ms = time_steps(step, steps, warm, dist_on)
     for e in eps:
         e.stats = {k: 0 for k in e.stats}
     st = stage_times(step, 1, 0)  # one step, per-stage times summed over its layers' local forwards
     local_ms = sum(st.values()) * n_layers   # stage_times averages over calls (n_layers per step)
+    if peer is not None:   # the exchange waits sit inside the permute and combine stages
+        local_ms -= (st.get("permute", 0.0) + st.get("combine", 0.0)) * n_layers
     recv = sum(e.stats["recv_rows"] for e in eps)
     a2a = sum(e.stats["a2a_bytes_out"] + e.stats["a2a_bytes_back"] for e in eps)
     t = torch.tensor([recv, a2a, local_ms], dtype=torch.float64, device=dev)
@@ -437,8 +448,10 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
                                     f"decode batch {total} tokens" if kind == "ep40" else
                                     f"BASELINE configs[4]: {total} tokens through {n_layers} MoE layers, Zipf(1.5) "
                                     "routing"),
-                       "parallelism": f"expert parallel over {world} GPU(s), {e_loc} experts each, {T} tokens per "
-                                      "GPU, NCCL all-to-all dispatch/combine" if world > 1 else "single GPU",
+                       "parallelism": (f"expert parallel over {world} GPU(s), {e_loc} experts each, {T} tokens per "
+                                       "GPU, " + ("dispatch/combine by peer loads inside the layer kernels (no NCCL)"
+                                                  if peer is not None else "NCCL all-to-all dispatch/combine"))
+                                      if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (every step streams the routed experts of all layers)"},
             "layer_tok_s": round(value * n_layers, 1),
             "ep": {"rows_per_gpu_per_step": [round(r, 1) for r in rows],
@@ -504,13 +517,14 @@ def main():
         return run_stack_workload(a, a.workload, world, rank, local, dev, dist_on, hbm, tf_burst, peak_src)
 
     from dsv41_flash_offload_b200 import exl3
-    from dsv41_flash_offload_b200.ep import EPMoE, local_layer_fn
+    from dsv41_flash_offload_b200.ep import EPMoE, EPPeerMoE, local_layer_fn
     e_loc = E // world
     lo, hi = rank * e_loc, (rank + 1) * e_loc
     # N > 1: expert parallelism -- this rank holds experts [lo, hi) of every layer and its own tokens
     layers = [exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, layer=l, device=dev,
                                           expert_range=(lo, hi) if world > 1 else None) for l in range(a.layers)]
-    eps = [EPMoE(local_layer_fn(lay, LIMIT), E) for lay in layers] if world > 1 else None
+    peer = EPPeerMoE(layers[0], E, T, TOPK, limit=LIMIT) if world > 1 and a.ep == "peer" else None
+    eps = [EPMoE(local_layer_fn(lay, LIMIT), E) for lay in layers] if world > 1 and peer is None else None
     for ep in eps or []:
         ep.slot_capacity = T  # every rank runs T-token decode batches: fixed-slot dispatch
     all_batches = [make_batches(T, a.batches, 1000 + 100 * r) for r in range(world)]
@@ -520,7 +534,9 @@ def main():
     fat = exl3.FAT_EXPERT_THRESHOLD
 
     def forward(i, x, ids, w, o):
-        if eps is None:
+        if peer is not None:
+            o.copy_(peer(x, ids, w, layer=layers[i % len(layers)]))
+        elif eps is None:
             exl3.apply_exl3_fused_moe(x, ids, w, layers[i % len(layers)], None, None, LIMIT, out=o)
         else:
             o.copy_(eps[i % len(eps)](x, ids, w))
@@ -560,7 +576,8 @@ def main():
     distinct = statistics.mean(d for _, d in gb)
     achieved = bytes_gu / (st["gemv_gateup"] / 1e3) / 1e9
     layer_gbs = statistics.mean(lb) / (ms / a.steps / 1e3) / 1e9
-    traffic = traffic_from_profile() if world == 1 else None  # the committed capture is the N=1 workload
+    ratio = traffic_ratio_from_profile() if world == 1 else None  # the committed capture is the N=1 workload
+    traffic = round(ratio * bytes_gu) if ratio else None
 
     # end to end through the public API with pinned host buffers
     hb = [(torch.from_numpy(x).to(torch.bfloat16).pin_memory(), torch.from_numpy(ids).pin_memory(),
@@ -596,16 +613,36 @@ def main():
                    "fat_threshold": fat},
         "roofline": {"bound": "hbm", "kernel": "exl3_gemv_kernel<0> (decode-GEMV gate/up + act + down-input)",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                     "traffic": traffic, "peak_source": f"{peak_src} hbm_gbs (copy bandwidth)",
+                     "traffic": traffic, "traffic_source": "profiles/gemv_gateup_decode_T64.txt DRAM/algorithmic "
+                     f"ratio {ratio} x bytes_per_launch" if ratio else None,
+                     "peak_source": f"{peak_src} hbm_gbs (copy bandwidth)",
                      "bytes_per_launch": round(bytes_gu), "distinct_experts_per_step": round(distinct, 1),
                      "avg_launch_ms": round(st["gemv_gateup"], 5)},
         "layer_hbm": {"achieved_gbs": round(layer_gbs, 1), "frac": round(layer_gbs / hbm, 4),
                       "bytes_per_step": round(statistics.mean(lb))},
         "stage_ms": {k: round(v, 5) for k, v in st.items()},
         "e2e": {"value": round(e2e_val, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": T * H * 4},
-        "gpu_launches": a.steps * launches_per_step(T, fat),
+        "gpu_launches": a.steps * (launches_per_step(world * T, fat) + 4 if peer is not None else launches_per_step(T, fat)),
         "clocks": clocks,
     }
+    if peer is not None:
+        # bytes pulled over NVLink per step by this rank: the token rows of the routes it serves (row
+        # transform) and the expert outputs of its own valid routes (combine)
+        pulled = []
+        for b in range(a.batches):
+            ids_all = [all_batches[r][b][1] for r in range(world)]
+            rows = sum(int(((i >= lo) & (i < hi)).sum()) for i in ids_all)
+            own = int(((ids_all[rank] >= 0) & (ids_all[rank] < E)).sum())
+            pulled.append((rows + own) * H * 2)
+        exch = st.get("permute", 0.0) + st.get("combine", 0.0)
+        line["ep"] = {"mode": "peer memory (EPPeerMoE): rows pulled by the row transform, outputs by the combine",
+                      "experts_per_gpu": e_loc, "peer_bytes_per_step": round(statistics.mean(pulled)),
+                      "step_ms": round(ms / a.steps, 5),
+                      "exchange_stages_ms": {"publish_gather_permute": round(st.get("permute", 0.0), 5),
+                                             "combine_pull": round(st.get("combine", 0.0), 5)},
+                      "exchange_and_permute_share": round(min(1.0, exch / (ms / a.steps)), 4)}
+        line["config"]["parallelism"] = (f"expert parallel over {world} GPUs ({e_loc} experts each, {T} tokens per "
+                                         "GPU), dispatch/combine by peer loads inside the layer kernels (no NCCL)")
     if eps is not None:
         calls = a.warmup + a.steps  # the e2e pass, counted since the stats were reset
         sent = sum(e.stats["sent_rows"] for e in eps) / calls

@@ -20,8 +20,12 @@ SYMBOLS = (
     "dsv41_last_error", "dsv41_abi_version", "dsv41_build_info", "dsv41_moe_workspace_size",
     "dsv41_moe_forward", "dsv41_moe_forward_noalloc", "dsv41_permute_workspace_size", "dsv41_permute", "dsv41_combine",
     "dsv41_decode_dense", "dsv41_expert_gemm", "dsv41_expert_gemm_workspace_size", "dsv41_read_status", "dsv41_wait_selftest",
+    "dsv41_ep_peer_buffer_size", "dsv41_ep_peer_alloc", "dsv41_ep_peer_open", "dsv41_ep_peer_close", "dsv41_ep_peer_free",
+    "dsv41_ep_peer_forward", "dsv41_ep_peer_read_status",
     "dsv41_set_stage_timing", "dsv41_read_stage_times",
 )
+MAX_PEERS = 8
+IPC_HANDLE_BYTES = 64
 N_STAGES = 7
 STAGE_NAMES = ("permute", "prep", "gemv_gateup", "gemm_gateup", "gemv_down", "gemm_down", "combine")
 
@@ -36,6 +40,11 @@ class MoeLayer(C.Structure):
 class MoeOptions(C.Structure):
     _fields_ = [("fat_threshold", C.c_int32), ("limit", C.c_float), ("expert_map", C.c_void_p),
                 ("map_len", C.c_int32), ("split_k", C.c_int32), ("max_routes", C.c_int32)]
+
+
+class EpPeerGroup(C.Structure):
+    _fields_ = [("rank", C.c_int32), ("world", C.c_int32), ("num_global_experts", C.c_int32),
+                ("tokens_cap", C.c_int32), ("bases", C.c_void_p * MAX_PEERS)]
 
 
 class Dsv41Error(RuntimeError):
@@ -86,6 +95,22 @@ def load(path: str | None = None):
         L.dsv41_read_status.argtypes = [vp, vp, C.POINTER(C.c_int32)]
         L.dsv41_wait_selftest.restype = C.c_int
         L.dsv41_wait_selftest.argtypes = [vp, C.c_uint32, vp]
+        gp = C.POINTER(EpPeerGroup)
+        L.dsv41_ep_peer_buffer_size.restype = C.c_int
+        L.dsv41_ep_peer_buffer_size.argtypes = [gp, C.POINTER(MoeLayer), i32, i32, C.POINTER(C.c_size_t)]
+        L.dsv41_ep_peer_alloc.restype = C.c_int
+        L.dsv41_ep_peer_alloc.argtypes = [C.c_size_t, C.POINTER(C.c_void_p), vp]
+        L.dsv41_ep_peer_open.restype = C.c_int
+        L.dsv41_ep_peer_open.argtypes = [vp, C.POINTER(C.c_void_p)]
+        L.dsv41_ep_peer_close.restype = C.c_int
+        L.dsv41_ep_peer_close.argtypes = [vp]
+        L.dsv41_ep_peer_free.restype = C.c_int
+        L.dsv41_ep_peer_free.argtypes = [vp]
+        L.dsv41_ep_peer_forward.restype = C.c_int
+        L.dsv41_ep_peer_forward.argtypes = [C.POINTER(MoeLayer), gp, C.c_uint32, vp, i32, i32, i64p, vp, i32,
+                                            C.c_float, i32, vp, vp]
+        L.dsv41_ep_peer_read_status.restype = C.c_int
+        L.dsv41_ep_peer_read_status.argtypes = [gp, C.POINTER(MoeLayer), i32, i32, vp, C.POINTER(C.c_int32)]
         L.dsv41_set_stage_timing.restype = C.c_int
         L.dsv41_set_stage_timing.argtypes = [i32]
         L.dsv41_read_stage_times.restype = C.c_int

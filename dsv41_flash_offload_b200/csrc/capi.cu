@@ -8,6 +8,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "../../include/dsv41_b200.h"
@@ -152,6 +153,55 @@ static PermBuffers perm_buffers(void* ws, const Layout& L)
     pb.status = at<int>(ws, L.status);
     pb.rows_cap = L.rows;
     return pb;
+}
+
+// ------------------------------------------------------------------------------------------
+// expert parallelism over peer memory: layout of each rank's shared buffer (same on all ranks)
+// ------------------------------------------------------------------------------------------
+constexpr size_t kCtrlInFlags = 0;     // uint32 in_flag[kMaxPeers]: step stamps written by peers
+constexpr size_t kCtrlOutFlags = 64;   // uint32 out_flag[kMaxPeers]
+constexpr size_t kCtrlStatus = 128;    // int status of the exchange waits
+
+struct PeerLayout {
+    size_t ctrl, x[2], ids[2], w[2], ids_loc[2], w_loc[2], ws[2], total;
+    Layout L;  // the local forward over world * tokens_cap tokens
+};
+
+static PeerLayout make_peer_layout(int world, int tcap, int k, int e_loc, int H, int I, int fat)
+{
+    PeerLayout P{};
+    P.L = make_layout(world * tcap, k, e_loc, H, I, 0, fat);
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = align_up(o + bytes, 256);
+        return at;
+    };
+    const size_t n = (size_t)tcap * k, nl = (size_t)world * tcap * k;
+    P.ctrl = take(256);
+    for (int p = 0; p < 2; ++p) {
+        P.x[p] = take((size_t)tcap * H * 2);
+        P.ids[p] = take(n * 4);
+        P.w[p] = take(n * 4);
+        P.ids_loc[p] = take(nl * 8);
+        P.w_loc[p] = take(nl * 4);
+        P.ws[p] = take(P.L.total);
+    }
+    P.total = o;
+    return P;
+}
+
+static int check_group(const dsv41_ep_peer_group* g)
+{
+    if (!g) return fail(DSV41_E_INVALID, "group is NULL");
+    if (g->world < 1 || g->world > kMaxPeers || g->rank < 0 || g->rank >= g->world)
+        return fail(DSV41_E_INVALID, "rank %d / world %d out of range (world 1..%d)", g->rank, g->world, kMaxPeers);
+    if (g->num_global_experts <= 0 || g->num_global_experts % g->world)
+        return fail(DSV41_E_INVALID, "%d experts do not shard over %d ranks", g->num_global_experts, g->world);
+    if (g->tokens_cap <= 0) return fail(DSV41_E_INVALID, "tokens_cap %d", g->tokens_cap);
+    for (int d = 0; d < g->world; ++d)
+        if (!g->bases[d]) return fail(DSV41_E_INVALID, "base of rank %d is NULL", d);
+    return DSV41_OK;
 }
 
 // run_batch semantics: listed experts with more rows than this use the tcgen05 GEMM, the rest the
@@ -351,6 +401,166 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     if ((err = launch_combine(y, pb.route_pos, weights, T, topk, H, 0, out, st)) != cudaSuccess)
         return cuda_fail(err, "combine");
     timer_end(st);
+    return DSV41_OK;
+}
+
+int dsv41_ep_peer_buffer_size(const dsv41_ep_peer_group* g, const dsv41_moe_layer* local_layer, int32_t topk,
+                               int32_t fat_threshold, size_t* bytes)
+{
+    int rc = check_group(g);
+    if (rc) return rc;
+    if ((rc = check_layer(local_layer))) return rc;
+    if (!bytes || topk <= 0) return fail(DSV41_E_INVALID, "bad topk %d or NULL bytes", topk);
+    if (local_layer->num_experts != g->num_global_experts / g->world)
+        return fail(DSV41_E_INVALID, "local layer has %d experts, expected %d", local_layer->num_experts,
+                    g->num_global_experts / g->world);
+    const int tl = g->world * g->tokens_cap;
+    const int fat = (fat_threshold >= 0 && tl > fat_threshold) ? fat_threshold : -1;
+    *bytes = make_peer_layout(g->world, g->tokens_cap, topk, local_layer->num_experts, local_layer->hidden,
+                              local_layer->intermediate, fat).total;
+    return DSV41_OK;
+}
+
+int dsv41_ep_peer_alloc(size_t bytes, void** base, void* ipc_handle)
+{
+    if (!base || !ipc_handle || bytes == 0) return fail(DSV41_E_INVALID, "bad arguments");
+    *base = nullptr;
+    cudaError_t err = cudaMalloc(base, bytes);
+    if (err != cudaSuccess) return cuda_fail(err, "peer buffer cudaMalloc");
+    if ((err = cudaMemset(*base, 0, bytes)) != cudaSuccess) {
+        cudaFree(*base);
+        *base = nullptr;
+        return cuda_fail(err, "peer buffer clear");
+    }
+    cudaIpcMemHandle_t h;
+    if ((err = cudaIpcGetMemHandle(&h, *base)) != cudaSuccess) {
+        cudaFree(*base);
+        *base = nullptr;
+        return cuda_fail(err, "cudaIpcGetMemHandle");
+    }
+    static_assert(sizeof(h) == DSV41_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(ipc_handle, &h, sizeof(h));
+    return DSV41_OK;
+}
+
+int dsv41_ep_peer_open(const void* ipc_handle, void** peer_base)
+{
+    if (!ipc_handle || !peer_base) return fail(DSV41_E_INVALID, "NULL pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    cudaError_t err = cudaIpcOpenMemHandle(peer_base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaIpcOpenMemHandle");
+    return DSV41_OK;
+}
+
+int dsv41_ep_peer_close(void* peer_base)
+{
+    if (!peer_base) return DSV41_OK;
+    cudaError_t err = cudaIpcCloseMemHandle(peer_base);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaIpcCloseMemHandle");
+    return DSV41_OK;
+}
+
+int dsv41_ep_peer_free(void* base)
+{
+    if (!base) return DSV41_OK;
+    cudaError_t err = cudaFree(base);
+    if (err != cudaSuccess) return cuda_fail(err, "peer buffer cudaFree");
+    return DSV41_OK;
+}
+
+int dsv41_ep_peer_forward(const dsv41_moe_layer* local_layer, const dsv41_ep_peer_group* g, uint32_t step,
+                          const void* x, int32_t x_dtype, int32_t T, const int64_t* ids, const float* weights,
+                          int32_t topk, float limit, int32_t fat_threshold, float* out, void* stream)
+{
+    int rc = check_group(g);
+    if (rc) return rc;
+    if ((rc = check_layer(local_layer))) return rc;
+    const int world = g->world, rank = g->rank, tcap = g->tokens_cap, k = topk;
+    const int E = g->num_global_experts, e_loc = E / world, H = local_layer->hidden, I = local_layer->intermediate;
+    if (local_layer->num_experts != e_loc)
+        return fail(DSV41_E_INVALID, "local layer has %d experts, expected %d", local_layer->num_experts, e_loc);
+    if (T < 0 || T > tcap || k <= 0) return fail(DSV41_E_INVALID, "T=%d (tokens_cap %d), topk=%d", T, tcap, k);
+    if (x_dtype < DSV41_DTYPE_F16 || x_dtype > DSV41_DTYPE_F32) return fail(DSV41_E_INVALID, "bad x_dtype %d", x_dtype);
+    if (T > 0 && (!x || !ids || !weights || !out)) return fail(DSV41_E_INVALID, "NULL input/output pointer");
+    const int tl = world * tcap;
+    const int fat = (fat_threshold >= 0 && tl > fat_threshold) ? fat_threshold : -1;
+    const PeerLayout P = make_peer_layout(world, tcap, k, e_loc, H, I, fat);
+    const Layout& L = P.L;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int p = (int)(step & 1u);
+    const uint32_t stamp = step + 1u;
+    PeerTable peers{};
+    for (int d = 0; d < world; ++d) peers.base[d] = g->bases[d];
+    uint8_t* own = static_cast<uint8_t*>(g->bases[rank]);
+    int* xstatus = reinterpret_cast<int*>(own + P.ctrl + kCtrlStatus);
+    void* ws = own + P.ws[p];
+    cudaError_t err;
+    timer_begin(st);  // stages as dsv41_moe_forward; permute includes publish + gather, combine the pull
+    // 1. publish this rank's tokens, then stamp in_flag[rank] on every peer
+    if ((err = launch_ep_publish(x, x_dtype, ids, weights, T, tcap, k, E, H, reinterpret_cast<__half*>(own + P.x[p]),
+                                 reinterpret_cast<int*>(own + P.ids[p]), reinterpret_cast<float*>(own + P.w[p]), st)) !=
+        cudaSuccess)
+        return cuda_fail(err, "ep publish");
+    if ((err = launch_ep_signal(peers, world, rank, P.ctrl + kCtrlInFlags, stamp, st)) != cudaSuccess)
+        return cuda_fail(err, "ep signal in");
+    // 2. every peer's routes that land on this rank's experts
+    int64_t* ids_loc = reinterpret_cast<int64_t*>(own + P.ids_loc[p]);
+    float* w_loc = reinterpret_cast<float*>(own + P.w_loc[p]);
+    if ((err = launch_ep_gather(peers, world, rank, tcap, k, rank * e_loc, (rank + 1) * e_loc, stamp,
+                                P.ctrl + kCtrlInFlags, P.ids[p], P.w[p], ids_loc, w_loc, xstatus, st)) != cudaSuccess)
+        return cuda_fail(err, "ep gather");
+    // 3. the local forward over world * tcap tokens, token rows read from their ranks
+    const PermBuffers pb = perm_buffers(ws, L);
+    if ((err = launch_permute(ids_loc, w_loc, L.N, k, e_loc, nullptr, 0, fat, pb, st)) != cudaSuccess)
+        return cuda_fail(err, "permute");
+    timer_mark(st, 1);
+    XRows xr{};
+    for (int d = 0; d < world; ++d) xr.base[d] = static_cast<const uint8_t*>(g->bases[d]) + P.x[p];
+    xr.per = tcap;
+    xr.n = world;
+    if ((err = launch_prep_rows(xr, DSV41_DTYPE_F16, pb.token_sorted, pb.expert_sorted, pb.nrows, L.rows,
+                                static_cast<const __half*>(local_layer->w13_suh), H, at<__half>(ws, L.xt_g),
+                                at<__half>(ws, L.xt_u), st)) != cudaSuccess)
+        return cuda_fail(err, "prep");
+    timer_mark(st, 2);
+    if ((err = run_expert_passes(local_layer, pb, at<__half>(ws, L.xt_g), at<__half>(ws, L.xt_u),
+                                 at<__half>(ws, L.xt_d), at<__half>(ws, L.y), at<float>(ws, L.partials),
+                                 at<int>(ws, L.counters), at<int>(ws, L.status), L.split, L.groups_bound, L.rows, limit,
+                                 fat, at<uint8_t>(ws, L.gemm), st)) != cudaSuccess)
+        return cuda_fail(err, "expert passes");
+    // 4. outputs ready: stamp out_flag[rank] on every peer; 5. pull this rank's routes' outputs
+    if ((err = launch_ep_signal(peers, world, rank, P.ctrl + kCtrlOutFlags, stamp, st)) != cudaSuccess)
+        return cuda_fail(err, "ep signal out");
+    if (T > 0 &&
+        (err = launch_ep_combine(peers, world, rank, tcap, k, e_loc, stamp, P.ctrl + kCtrlOutFlags,
+                                 reinterpret_cast<const int*>(own + P.ids[p]), reinterpret_cast<const float*>(own + P.w[p]),
+                                 T, H, P.ws[p] + L.route_pos, P.ws[p] + L.y, out, xstatus, st)) != cudaSuccess)
+        return cuda_fail(err, "ep combine");
+    timer_end(st);
+    return DSV41_OK;
+}
+
+int dsv41_ep_peer_read_status(const dsv41_ep_peer_group* g, const dsv41_moe_layer* local_layer, int32_t topk,
+                              int32_t fat_threshold, void* stream, int32_t* status)
+{
+    int rc = check_group(g);
+    if (rc) return rc;
+    if ((rc = check_layer(local_layer))) return rc;
+    if (!status) return fail(DSV41_E_INVALID, "status is NULL");
+    const int tl = g->world * g->tokens_cap;
+    const int fat = (fat_threshold >= 0 && tl > fat_threshold) ? fat_threshold : -1;
+    const PeerLayout P = make_peer_layout(g->world, g->tokens_cap, topk, local_layer->num_experts, local_layer->hidden,
+                                          local_layer->intermediate, fat);
+    uint8_t* own = static_cast<uint8_t*>(g->bases[g->rank]);
+    int worst = 0;
+    const size_t words[3] = {P.ctrl + kCtrlStatus, P.ws[0] + P.L.status, P.ws[1] + P.L.status};
+    for (size_t off : words) {
+        int32_t v = 0;
+        if ((rc = dsv41_read_status(own + off, stream, &v))) return rc;
+        if (v > worst) worst = v;
+    }
+    *status = worst;
     return DSV41_OK;
 }
 

@@ -9,6 +9,7 @@
 // B fragments in registers and the decoded weights never touch memory.
 #pragma once
 #include <cuda_fp16.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -167,6 +168,40 @@ __device__ __forceinline__ float act_gu(float g, float u, float limit)
         s = fminf(s, limit);
     }
     return __fmul_rn(s, u);
+}
+
+// 4-element row loads/stores (fp16 storage; inputs of any of the three ABI dtypes rounded to fp16)
+__device__ __forceinline__ void load4_as_half(const void* x, int dtype, size_t idx, float (&v)[4])
+{
+    if (dtype == 0) {
+        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __half*>(x) + idx);
+        const __half2 a = u32_as_half2(u.x), b = u32_as_half2(u.y);
+        v[0] = __low2float(a); v[1] = __high2float(a); v[2] = __low2float(b); v[3] = __high2float(b);
+    } else if (dtype == 1) {
+        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(x) + idx);
+        v[0] = __uint_as_float(u.x << 16); v[1] = __uint_as_float(u.x & 0xffff0000u);
+        v[2] = __uint_as_float(u.y << 16); v[3] = __uint_as_float(u.y & 0xffff0000u);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[q] = r16(v[q]);
+    } else {
+        const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + idx);
+        v[0] = r16(f.x); v[1] = r16(f.y); v[2] = r16(f.z); v[3] = r16(f.w);
+    }
+}
+
+__device__ __forceinline__ void load4_half(const __half* p, float (&v)[4])
+{
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __half2 a = u32_as_half2(u.x), b = u32_as_half2(u.y);
+    v[0] = __low2float(a); v[1] = __high2float(a); v[2] = __low2float(b); v[3] = __high2float(b);
+}
+
+__device__ __forceinline__ void store4_half(__half* p, const float (&v)[4])
+{
+    uint2 u;
+    u.x = half2_as_u32(__floats2half2_rn(v[0], v[1]));
+    u.y = half2_as_u32(__floats2half2_rn(v[2], v[3]));
+    *reinterpret_cast<uint2*>(p) = u;
 }
 
 // ------------------------------------------------------------------------------------------

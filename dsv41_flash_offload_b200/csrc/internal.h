@@ -11,6 +11,17 @@ constexpr int kRowsPerGroup = 16;     // decode-GEMV row group (one mma M tile)
 constexpr int kPermSmallMax = 8192;   // routes handled by the single-CTA permutation
 constexpr int kPermSegment = 256;     // routes per warp segment in the multi-CTA permutation
 constexpr int kMaxExperts = 4096;
+constexpr int kMaxPeers = 8;     // expert-parallel ranks reachable by peer loads
+
+// device base pointers of every rank's shared buffer (index = rank), passed by value to kernels
+struct PeerTable {
+    void* base[kMaxPeers];
+};
+// where the row transform reads token t: n == 1: base[0] + t rows; else base[t / per] + (t % per) rows
+struct XRows {
+    const void* base[kMaxPeers];
+    int per, n;
+};
 
 // Routing permutation results (device pointers; int32 internally)
 struct PermBuffers {
@@ -44,6 +55,19 @@ cudaError_t launch_permute(const int64_t* ids, const float* weights, int N, int 
 cudaError_t launch_prep(const void* x, int x_dtype, const int* token_sorted, const int* expert_sorted,
                         const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
                         cudaStream_t st);
+cudaError_t launch_prep_rows(const XRows& x, int x_dtype, const int* token_sorted, const int* expert_sorted,
+                             const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
+                             cudaStream_t st);
+cudaError_t launch_ep_publish(const void* x, int x_dtype, const int64_t* ids, const float* w, int T, int tcap, int k,
+                              int E, int H, __half* X, int* IDS, float* W, cudaStream_t st);
+cudaError_t launch_ep_signal(const PeerTable& peers, int world, int rank, size_t flag_off, uint32_t stamp,
+                             cudaStream_t st);
+cudaError_t launch_ep_gather(const PeerTable& peers, int world, int rank, int tcap, int k, int lo, int hi,
+                             uint32_t stamp, size_t in_flags_off, size_t ids_off, size_t w_off, int64_t* ids_loc,
+                             float* w_loc, int* status, cudaStream_t st);
+cudaError_t launch_ep_combine(const PeerTable& peers, int world, int rank, int tcap, int k, int e_loc, uint32_t stamp,
+                              size_t out_flags_off, const int* ids, const float* w, int T, int H, size_t route_pos_off,
+                              size_t y_off, float* out, int* status, cudaStream_t st);
 
 // Work lists for an explicit expert list over caller-permuted rows (run_batch semantics):
 // int32 counts/offsets copies, expert_sorted (-1 for rows of unlisted experts), GEMV groups of the

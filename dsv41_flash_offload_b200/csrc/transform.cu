@@ -9,46 +9,11 @@
 #include "common.cuh"
 #include "internal.h"
 
-#include <cuda_bf16.h>
-
 namespace dsv41 {
-
-__device__ __forceinline__ void load4_as_half(const void* x, int dtype, size_t idx, float (&v)[4])
-{
-    if (dtype == 0) {
-        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __half*>(x) + idx);
-        const __half2 a = u32_as_half2(u.x), b = u32_as_half2(u.y);
-        v[0] = __low2float(a); v[1] = __high2float(a); v[2] = __low2float(b); v[3] = __high2float(b);
-    } else if (dtype == 1) {
-        const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(x) + idx);
-        v[0] = __uint_as_float(u.x << 16); v[1] = __uint_as_float(u.x & 0xffff0000u);
-        v[2] = __uint_as_float(u.y << 16); v[3] = __uint_as_float(u.y & 0xffff0000u);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) v[q] = r16(v[q]);
-    } else {
-        const float4 f = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + idx);
-        v[0] = r16(f.x); v[1] = r16(f.y); v[2] = r16(f.z); v[3] = r16(f.w);
-    }
-}
-
-__device__ __forceinline__ void load4_half(const __half* p, float (&v)[4])
-{
-    const uint2 u = *reinterpret_cast<const uint2*>(p);
-    const __half2 a = u32_as_half2(u.x), b = u32_as_half2(u.y);
-    v[0] = __low2float(a); v[1] = __high2float(a); v[2] = __low2float(b); v[3] = __high2float(b);
-}
-
-__device__ __forceinline__ void store4_half(__half* p, const float (&v)[4])
-{
-    uint2 u;
-    u.x = half2_as_u32(__floats2half2_rn(v[0], v[1]));
-    u.y = half2_as_u32(__floats2half2_rn(v[2], v[3]));
-    *reinterpret_cast<uint2*>(p) = u;
-}
 
 // one warp task = (sorted row p, 128-block b): both gate and up transforms of that block
 // rows p < *nrows; rows whose expert_sorted entry is negative are skipped
-__global__ void __launch_bounds__(256) prep_kernel(const void* x, int x_dtype, const int* token_sorted,
+__global__ void __launch_bounds__(256) prep_kernel(const XRows x, int x_dtype, const int* token_sorted,
                                                    const int* expert_sorted, const int* nrows,
                                                    const __half* w13_suh, int H, __half* xt_g, __half* xt_u)
 {
@@ -64,7 +29,14 @@ __global__ void __launch_bounds__(256) prep_kernel(const void* x, int x_dtype, c
         const int t = token_sorted[p];
         const int c = b * 128 + lane * 4;
         float xv[4];
-        load4_as_half(x, x_dtype, (size_t)t * H + c, xv);
+        // token t's row: the caller's rows, or (expert parallel) row t % per of rank t / per
+        const void* xb = x.base[0];
+        size_t row = (size_t)t;
+        if (x.n > 1) {
+            xb = x.base[t / x.per];
+            row = (size_t)(t % x.per);
+        }
+        load4_as_half(xb, x_dtype, row * H + c, xv);
 #pragma unroll
         for (int m = 0; m < 2; ++m) {
             float s[4], v[4];
@@ -82,6 +54,17 @@ __global__ void __launch_bounds__(256) prep_kernel(const void* x, int x_dtype, c
 cudaError_t launch_prep(const void* x, int x_dtype, const int* token_sorted, const int* expert_sorted,
                         const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
                         cudaStream_t st)
+{
+    XRows xr{};
+    xr.base[0] = x;
+    xr.per = 1;
+    xr.n = 1;
+    return launch_prep_rows(xr, x_dtype, token_sorted, expert_sorted, nrows, N, w13_suh, H, xt_g, xt_u, st);
+}
+
+cudaError_t launch_prep_rows(const XRows& x, int x_dtype, const int* token_sorted, const int* expert_sorted,
+                             const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
+                             cudaStream_t st)
 {
     const long long tasks = (long long)N * (H / 128);
     long long blocks = (tasks + 7) / 8;

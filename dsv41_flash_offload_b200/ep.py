@@ -18,6 +18,7 @@ tested on CPU ranks (gloo) with a stand-in expert.
 """
 from __future__ import annotations
 
+import ctypes as C
 from typing import Callable
 
 import torch
@@ -150,3 +151,126 @@ def local_layer_fn(layer, limit: float | None = 10.0, fat_threshold: int | None 
                                     max_routes=max_routes)
 
     return fn
+
+
+class EPPeerMoE:
+    """Expert parallelism over NVLink peer memory, no collective library on the data path.
+
+    Each rank holds `layer` = its shard of E/world experts (global expert e on rank e // (E/world)).
+    Construction is collective over `group` (every rank must construct with the same arguments): the
+    ranks allocate one shared device buffer each, exchange CUDA IPC handles over the process group
+    (host side only) and map each other's buffers. A call runs one layer step for this rank's
+    T <= tokens_cap tokens: the row transform pulls each routed token row from its rank and the
+    combine pulls each expert output from the rank that computed it, both by plain peer loads,
+    ordered by step stamps in the shared buffers (bounded device waits; `read_status()` reports an
+    expired wait). Every rank must call once per step, in the same order. No host synchronisation:
+    steps of equal parity can be captured in one CUDA graph.
+    """
+
+    def __init__(self, layer, num_global_experts: int, tokens_cap: int, topk: int, group=None,
+                 limit: float | None = 10.0, fat_threshold: int | None = None):
+        from . import _lib, exl3
+        self.layer = layer
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > _lib.MAX_PEERS:
+            raise ValueError(f"world {self.world} > {_lib.MAX_PEERS} peer ranks")
+        e_here = layer._exl3_num_experts
+        if num_global_experts % self.world or e_here != num_global_experts // self.world:
+            raise ValueError(f"layer holds {e_here} experts; expected {num_global_experts} / {self.world}")
+        self.E, self.tokens_cap, self.topk, self.group = int(num_global_experts), int(tokens_cap), int(topk), group
+        self.limit = 0.0 if limit is None else float(limit)
+        self.fat = exl3.FAT_EXPERT_THRESHOLD if fat_threshold is None else int(fat_threshold)
+        self.device = layer.device
+        self.step = 0
+        L = _lib.load()
+        self._L = L
+        g = _lib.EpPeerGroup()
+        g.rank, g.world, g.num_global_experts, g.tokens_cap = self.rank, self.world, self.E, self.tokens_cap
+        self._g = g
+        # sizes only depend on the arguments, so every rank computes the same layout
+        for d in range(self.world):
+            g.bases[d] = 1
+        nbytes = C.c_size_t()
+        with torch.cuda.device(self.device):
+            _lib.check(L.dsv41_ep_peer_buffer_size(C.byref(g), C.byref(layer._c), self.topk, self.fat,
+                                                   C.byref(nbytes)), "ep_peer_buffer_size")
+            base = C.c_void_p()
+            handle = (C.c_uint8 * _lib.IPC_HANDLE_BYTES)()
+            _lib.check(L.dsv41_ep_peer_alloc(nbytes.value, C.byref(base), handle), "ep_peer_alloc")
+        self.nbytes = nbytes.value
+        self._own = base.value
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        else:
+            handles[0] = bytes(handle)
+        self._opened = []
+        with torch.cuda.device(self.device):
+            for d in range(self.world):
+                if d == self.rank:
+                    g.bases[d] = self._own
+                    continue
+                h = (C.c_uint8 * _lib.IPC_HANDLE_BYTES).from_buffer_copy(handles[d])
+                pb = C.c_void_p()
+                _lib.check(L.dsv41_ep_peer_open(h, C.byref(pb)), f"ep_peer_open(rank {d})")
+                g.bases[d] = pb.value
+                self._opened.append(pb.value)
+        if self.world > 1:
+            dist.barrier(group=group)   # every buffer is mapped before any rank signals into it
+        self.stats = {"steps": 0}
+
+    def __call__(self, x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, layer=None) -> torch.Tensor:
+        """One step; `layer` optionally replaces the local shard for this call (another layer of the same
+        shape, e.g. the next layer of a stack sharing these buffers)."""
+        from . import _lib, exl3
+        layer = self.layer if layer is None else layer
+        if layer._exl3_num_experts != self.layer._exl3_num_experts or layer.w13_suh.shape != self.layer.w13_suh.shape \
+                or layer.w13_svh.shape != self.layer.w13_svh.shape:
+            raise ValueError("layer shape differs from the one the buffers were sized for")
+        T, H = x2d.shape
+        if T > self.tokens_cap:
+            raise ValueError(f"{T} tokens > tokens_cap {self.tokens_cap}")
+        ids = ids.reshape(T, -1)
+        if ids.shape[1] != self.topk:
+            raise ValueError(f"topk {ids.shape[1]} != {self.topk}")
+        ids = ids.to(torch.int64).contiguous()
+        weights = weights.reshape(T, self.topk).to(torch.float32).contiguous()
+        x2d = x2d.contiguous()
+        out = torch.empty((T, H), dtype=torch.float32, device=x2d.device)
+        stream = torch.cuda.current_stream(x2d.device)
+        with torch.cuda.device(x2d.device):
+            _lib.check(self._L.dsv41_ep_peer_forward(
+                C.byref(layer._c), C.byref(self._g), self.step & 0xFFFFFFFF, x2d.data_ptr(),
+                exl3._DTYPES[x2d.dtype], T, ids.data_ptr(), weights.data_ptr(), self.topk, self.limit, self.fat,
+                out.data_ptr(), C.c_void_p(stream.cuda_stream)), "ep_peer_forward")
+        self.step += 1
+        self.stats["steps"] += 1
+        return out
+
+    def read_status(self) -> int:
+        """Synchronise; 0 = ok, 1 = a bounded device wait (peer stamp or pipeline) ran out."""
+        st = C.c_int32()
+        stream = torch.cuda.current_stream(self.device)
+        with torch.cuda.device(self.device):
+            from . import _lib
+            _lib.check(self._L.dsv41_ep_peer_read_status(C.byref(self._g), C.byref(self.layer._c), self.topk, self.fat,
+                                                         C.c_void_p(stream.cuda_stream), C.byref(st)),
+                       "ep_peer_read_status")
+        return st.value
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers and free this rank's once every rank is done."""
+        if self._own is None:
+            return
+        from . import _lib
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for pb in self._opened:
+                _lib.check(self._L.dsv41_ep_peer_close(C.c_void_p(pb)), "ep_peer_close")
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            _lib.check(self._L.dsv41_ep_peer_free(C.c_void_p(self._own)), "ep_peer_free")
+        self._opened, self._own = [], None

@@ -157,6 +157,41 @@ int dsv41_read_status(const void* workspace, void* stream, int32_t* status);
  * Read it with dsv41_read_status; the stream and context stay usable. */
 int dsv41_wait_selftest(void* workspace, uint32_t limit_us, void* stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Expert parallelism over NVLink peer memory (no counterpart in the reference, which runs one GPU
+ * with experts in host RAM, docker/entrypoint.sh:135-140). Experts are sharded: global expert e
+ * lives on rank e / (num_global_experts / world). Each rank allocates one shared buffer
+ * (dsv41_ep_peer_alloc: cudaMalloc + cudaIpcGetMemHandle), exchanges the 64-byte handles with its
+ * peers over the host, opens theirs (dsv41_ep_peer_open) and fills bases[] (own buffer at
+ * bases[rank]). dsv41_ep_peer_forward then runs one step of the layer for this rank's T <=
+ * tokens_cap tokens with no collective library: the row transform reads each routed token row
+ * from its rank and the combine reads each expert output from the rank that computed it, both by
+ * plain peer loads; step stamps in the shared buffers order the ranks (bounded waits, status 1
+ * on expiry -> dsv41_ep_peer_read_status). Every rank must call it once per step with the same
+ * `step` sequence (0, 1, 2, ...), topk and tokens_cap. The buffers alternate by step parity, so a
+ * CUDA graph of one step replays only for steps of the same parity.
+ * ------------------------------------------------------------------------------------------ */
+#define DSV41_MAX_PEERS 8
+#define DSV41_IPC_HANDLE_BYTES 64
+typedef struct dsv41_ep_peer_group {
+    int32_t rank, world;            /* world <= DSV41_MAX_PEERS */
+    int32_t num_global_experts;     /* divisible by world */
+    int32_t tokens_cap;             /* max tokens per rank and step (same on every rank) */
+    void* bases[DSV41_MAX_PEERS];   /* device address of each rank's shared buffer in this process */
+} dsv41_ep_peer_group;
+
+int dsv41_ep_peer_buffer_size(const dsv41_ep_peer_group* group, const dsv41_moe_layer* local_layer, int32_t topk,
+                              int32_t fat_threshold, size_t* bytes);
+int dsv41_ep_peer_alloc(size_t bytes, void** base, void* ipc_handle);
+int dsv41_ep_peer_open(const void* ipc_handle, void** peer_base);
+int dsv41_ep_peer_close(void* peer_base);
+int dsv41_ep_peer_free(void* base);
+int dsv41_ep_peer_forward(const dsv41_moe_layer* local_layer, const dsv41_ep_peer_group* group, uint32_t step,
+                          const void* x, int32_t x_dtype, int32_t T, const int64_t* ids, const float* weights,
+                          int32_t topk, float limit, int32_t fat_threshold, float* out, void* stream);
+int dsv41_ep_peer_read_status(const dsv41_ep_peer_group* group, const dsv41_moe_layer* local_layer, int32_t topk,
+                              int32_t fat_threshold, void* stream, int32_t* status);
+
 /* Profiling (no counterpart in the reference; used by bench.py to time each kernel on the stream
  * it runs on). While enabled, dsv41_moe_forward records CUDA events at its stage boundaries for up
  * to DSV41_TIMING_MAX_CALLS calls (not under stream capture). dsv41_read_stage_times synchronises

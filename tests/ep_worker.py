@@ -2,7 +2,8 @@
 
 Each rank holds its shard E/world of a synthetic BASELINE-shape layer and routes its own 64 tokens over
 all global experts; the expert-parallel output (NCCL all-to-all dispatch/combine) must match the
-single-GPU layer (every rank also builds the full layer) within the parity bar."""
+single-GPU layer (every rank also builds the full layer) within the parity bar; then the same for
+the peer-memory path (EPPeerMoE: token rows and expert outputs read from peers, no collective)."""
 import datetime
 import os
 import sys
@@ -17,7 +18,7 @@ sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 from conftest import assert_close_layer  # noqa: E402
 from dsv41_flash_offload_b200 import exl3, synth  # noqa: E402
-from dsv41_flash_offload_b200.ep import EPMoE, local_layer_fn  # noqa: E402
+from dsv41_flash_offload_b200.ep import EPMoE, EPPeerMoE, local_layer_fn  # noqa: E402
 
 E, H, I, K, T = 384, 4096, 2048, 8, 64
 
@@ -48,8 +49,27 @@ def main():
         torch.cuda.synchronize()
         assert_close_layer(out.cpu().numpy(), ref.cpu().numpy(), f"rank {rank} case {case}")
     assert exl3.read_status(device=dev) == 0
+    # peer-memory expert parallelism (no collective on the data path): three steps cover both
+    # buffer parities; rank 1 runs fewer tokens than the capacity; invalid ids and empty rows
+    peer = EPPeerMoE(shard, E, tokens_cap=T, topk=K, limit=10.0)
+    for case in range(3):
+        seed = 700 + 10 * case + rank
+        Tc = T if (rank == 0 or case != 1) else 40
+        x = torch.from_numpy(synth.hidden_np(seed, Tc, H)).to(dev, torch.bfloat16)
+        ids_np, w_np = synth.routing_np(seed, Tc, E, K, kind="zipf" if case == 2 else "uniform", zipf_s=1.5)
+        ids, w = torch.from_numpy(ids_np).to(dev), torch.from_numpy(w_np).to(dev)
+        if case == 1:
+            ids[0, :] = -1
+            ids[2, 5] = E + 3
+        out = peer(x, ids, w)
+        ref = exl3.apply_exl3_fused_moe(x, ids, w, full, None, None, 10.0)
+        torch.cuda.synchronize()
+        assert_close_layer(out.cpu().numpy(), ref.cpu().numpy(), f"peer rank {rank} case {case}")
+    assert peer.read_status() == 0
+    peer.close()
     dist.barrier()
-    print(f"rank {rank}/{world} ok: sent {ep.stats['sent_rows']} rows, received {ep.stats['recv_rows']}", flush=True)
+    print(f"rank {rank}/{world} ok: sent {ep.stats['sent_rows']} rows, received {ep.stats['recv_rows']}; "
+          f"peer steps {peer.stats['steps']}", flush=True)
     dist.destroy_process_group()
 
 

@@ -162,3 +162,32 @@ def test_layer_validation_on_cpu_tensors():
         Exl3MoELayer(w13, w2, s(E, 2, H), s(E, 2, I + 16), s(E, I), s(E, H))
     with pytest.raises(ValueError):
         Exl3MoELayer(w13, w2.float(), s(E, 2, H), s(E, 2, I), s(E, I), s(E, H))
+
+
+def test_ep_peer_buffer_layout_host_checks():
+    """dsv41_ep_peer_buffer_size is pure host arithmetic (no device call): same size for every rank,
+    growing with world and tokens_cap, and argument errors for bad groups."""
+    import ctypes as C
+    from dsv41_flash_offload_b200 import _lib
+    L = _lib.load()
+    layer = _lib.MoeLayer(192, 4096, 2048, 0, *([16] * 7))   # dummy non-null pointers: never dereferenced
+
+    def size(world, rank, cap, E=384, topk=8):
+        g = _lib.EpPeerGroup()
+        g.rank, g.world, g.num_global_experts, g.tokens_cap = rank, world, E, cap
+        for d in range(_lib.MAX_PEERS):
+            g.bases[d] = 16
+        lay = _lib.MoeLayer(E // world if world and E % world == 0 else 1, 4096, 2048, 0, *([16] * 7))
+        n = C.c_size_t()
+        rc = L.dsv41_ep_peer_buffer_size(C.byref(g), C.byref(lay), topk, 32, C.byref(n))
+        return rc, n.value
+
+    sizes = [size(2, r, 64) for r in range(2)]
+    assert all(rc == 0 for rc, _ in sizes) and sizes[0][1] == sizes[1][1] > 0
+    assert size(4, 3, 64)[1] > size(2, 0, 64)[1]        # more peers -> more routes to hold
+    assert size(2, 0, 128)[1] > size(2, 0, 64)[1]
+    assert size(9, 0, 64)[0] == _lib.E_INVALID           # more than DSV41_MAX_PEERS ranks
+    assert size(2, 2, 64)[0] == _lib.E_INVALID           # rank out of range
+    assert size(5, 0, 64, E=384)[0] == _lib.E_INVALID    # 384 experts do not shard over 5
+    assert size(2, 0, 0)[0] == _lib.E_INVALID            # no capacity
+    del layer
