@@ -102,7 +102,7 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while running."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -112,7 +112,7 @@ class ClockSampler:
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200", "-i", gpu_id], stdout=self.f, stderr=subprocess.DEVNULL)
+                                       "-lms", "50", "-i", gpu_id], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
 
@@ -422,7 +422,14 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
         return x
 
     steps, warm = (max(1, min(a.steps, 10)) if kind == "ep40" else max(1, min(a.steps, 3))), 3
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid).replace("GPU-", "")
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid or str(local))
     ms = time_steps(step, steps, warm, dist_on)
+    clocks = sampler.stop()
     for e in eps:
         e.stats = {k: 0 for k in e.stats}
     st = stage_times(step, 1, 0)  # one step, per-stage times summed over its layers' local forwards
@@ -431,6 +438,19 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
         local_ms -= (st.get("permute", 0.0) + st.get("combine", 0.0)) * n_layers
     recv = sum(e.stats["recv_rows"] for e in eps)
     a2a = sum(e.stats["a2a_bytes_out"] + e.stats["a2a_bytes_back"] for e in eps)
+    if peer is not None:
+        # routes each rank serves (summed over all ranks' tokens and all layers) and the bytes this rank
+        # pulls: token rows of the routes it serves + expert outputs of its own valid routes
+        dest = torch.zeros(world, dtype=torch.float64, device=dev)
+        own = 0
+        for ids, _ in routes:
+            v = ids[(ids >= 0) & (ids < E)]
+            dest += torch.bincount(v // e_loc, minlength=world)[:world].double()
+            own += int(v.numel())
+        if dist_on:
+            torch.distributed.all_reduce(dest)
+        recv = float(dest[rank])
+        a2a = (recv + own) * H * 2
     t = torch.tensor([recv, a2a, local_ms], dtype=torch.float64, device=dev)
     allv = [torch.zeros_like(t) for _ in range(world)]
     if dist_on:
@@ -453,10 +473,13 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
                                                   if peer is not None else "NCCL all-to-all dispatch/combine"))
                                       if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (every step streams the routed experts of all layers)"},
-            "layer_tok_s": round(value * n_layers, 1),
-            "ep": {"rows_per_gpu_per_step": [round(r, 1) for r in rows],
+            "layer_tok_s": round(value * n_layers, 1), "clocks": clocks,
+            "ep": {"exchange": "peer memory" if peer is not None else "NCCL all-to-all",
+                   ("routes_served_per_gpu_per_step" if peer is not None else "rows_per_gpu_per_step"):
+                       [round(r, 1) for r in rows],
                    "max_over_mean_rows": round(max(rows) / max(statistics.mean(rows), 1e-9), 3),
-                   "a2a_bytes_per_step": [round(float(v[1])) for v in allv],
+                   ("peer_bytes_per_step" if peer is not None else "a2a_bytes_per_step"):
+                       [round(float(v[1])) for v in allv],
                    "local_moe_ms_per_step": [round(float(v[2]), 3) for v in allv],
                    "a2a_and_dispatch_share": round(max(0.0, 1.0 - max(float(v[2]) for v in allv) / (ms / steps)), 4)}}
     if rank == 0:
@@ -550,9 +573,11 @@ def main():
         uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid).replace("GPU-", "")
     except Exception:
         pass
+    # clocks are sampled from the first timed step through the end-to-end timed steps (two timed
+    # regions of K steps and the stage-timing pass between them): short steps at large N leave too
+    # few 50 ms samples inside one region alone
     sampler = ClockSampler(uuid or str(local))
     ms = time_steps(step, a.steps, a.warmup, dist_on)
-    clocks = sampler.stop()
     value = world * T * a.steps / (ms / 1e3)
 
     # dominant kernel: per-stage events over the same steps
@@ -594,6 +619,8 @@ def main():
         out_host.copy_(out, non_blocking=True)
 
     e2e_ms = time_steps(e2e_step, a.steps, a.warmup, dist_on)
+    clocks = sampler.stop()
+    clocks["window"] = "timed steps, stage-timing pass and end-to-end timed steps"
     e2e_val = world * T * a.steps / (e2e_ms / 1e3)
     h2d = hb[0][0].numel() * 2 + hb[0][1].numel() * 8 + hb[0][2].numel() * 4
 
