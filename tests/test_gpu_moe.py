@@ -246,3 +246,25 @@ def test_run_batch_mirror_vs_oracle(oracle, layer_small):
     wb[~keep] = 0.0
     ref = oracle_out(oracle, layer_small, x, ids, wb, LIMIT)
     assert_close_layer(out.cpu().numpy(), ref, "run_batch")
+
+
+def test_vllm_plugin_and_decode_graphs(layer_small):
+    """The installed module function on a vLLM-style layer (parameters only) equals the direct call;
+    DecodeGraphs replays are bit-identical to eager calls for batch sizes on and between the captured ones."""
+    import types
+    from dsv41_flash_offload_b200 import vllm_plugin
+    X = types.ModuleType("fake_vllm_exl3")
+    X.apply_exl3_fused_moe = lambda *a, **k: None
+    vllm_plugin.install(X)
+    vl = types.SimpleNamespace(**{n: torch.nn.Parameter(getattr(layer_small, n), requires_grad=False)
+                                  for n in ("w13_trellis", "w2_trellis", "w13_suh", "w13_svh", "w2_suh", "w2_svh")})
+    x, ids, w = _inputs(51, 9, 512, 16, 6)
+    got = X.apply_exl3_fused_moe(x, ids, w, vl, None, None, LIMIT)
+    ref = exl3.apply_exl3_fused_moe(x, ids, w, layer_small, None, None, LIMIT)
+    assert torch.equal(got, ref)
+    dg = vllm_plugin.DecodeGraphs(layer_small, sizes=(1, 4, 16), topk=6, limit=LIMIT)
+    for t, seed in ((1, 52), (3, 53), (16, 54), (11, 55)):
+        x, ids, w = _inputs(seed, t, 512, 16, 6)
+        out = dg(x, ids, w)
+        assert torch.equal(out, exl3.apply_exl3_fused_moe(x, ids, w, layer_small, None, None, LIMIT)), t
+    dg.close()

@@ -191,3 +191,36 @@ def test_ep_peer_buffer_layout_host_checks():
     assert size(5, 0, 64, E=384)[0] == _lib.E_INVALID    # 384 experts do not shard over 5
     assert size(2, 0, 0)[0] == _lib.E_INVALID            # no capacity
     del layer
+
+
+def test_vllm_plugin_install_uninstall_on_module():
+    """install() swaps the module's apply_exl3_fused_moe and wraps Exl3MoEMethod's
+    process_weights_after_loading (original first, then the B200 view), idempotently; uninstall
+    restores both (the reference's install(X) pattern, ct/ct_vllm.py:446-456)."""
+    import types
+    from dsv41_flash_offload_b200 import exl3, vllm_plugin
+
+    calls = []
+
+    class Exl3MoEMethod:
+        def process_weights_after_loading(self, layer):
+            calls.append("orig")
+
+    def orig_fused(*a, **k):
+        return "orig"
+
+    X = types.ModuleType("fake_vllm_exl3")
+    X.apply_exl3_fused_moe = orig_fused
+    X.Exl3MoEMethod = Exl3MoEMethod
+    vllm_plugin.install(X)
+    vllm_plugin.install(X)   # second call is a no-op
+    assert X.apply_exl3_fused_moe is not orig_fused
+    assert X.apply_exl3_fused_moe.__doc__ == exl3.apply_exl3_fused_moe.__doc__
+    layer = types.SimpleNamespace(_dsv41="view")   # as_layer returns the cached view
+    Exl3MoEMethod().process_weights_after_loading(layer)
+    assert calls == ["orig"]
+    vllm_plugin.uninstall(X)
+    assert X.apply_exl3_fused_moe is orig_fused
+    assert X.Exl3MoEMethod.process_weights_after_loading.__name__ == "process_weights_after_loading"
+    Exl3MoEMethod().process_weights_after_loading(layer)
+    assert calls == ["orig", "orig"]
