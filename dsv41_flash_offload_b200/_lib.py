@@ -20,6 +20,7 @@ SYMBOLS = (
     "dsv41_last_error", "dsv41_abi_version", "dsv41_build_info", "dsv41_moe_workspace_size",
     "dsv41_moe_forward", "dsv41_moe_forward_noalloc", "dsv41_permute_workspace_size", "dsv41_permute", "dsv41_combine",
     "dsv41_decode_dense", "dsv41_expert_gemm", "dsv41_expert_gemm_workspace_size", "dsv41_read_status", "dsv41_wait_selftest",
+    "dsv41_router_topk", "dsv41_moe_forward_logits",
     "dsv41_ep_peer_buffer_size", "dsv41_ep_peer_alloc", "dsv41_ep_peer_open", "dsv41_ep_peer_close", "dsv41_ep_peer_free",
     "dsv41_ep_peer_forward", "dsv41_ep_peer_read_status",
     "dsv41_set_stage_timing", "dsv41_read_stage_times",
@@ -40,6 +41,11 @@ class MoeLayer(C.Structure):
 class MoeOptions(C.Structure):
     _fields_ = [("fat_threshold", C.c_int32), ("limit", C.c_float), ("expert_map", C.c_void_p),
                 ("map_len", C.c_int32), ("split_k", C.c_int32), ("max_routes", C.c_int32)]
+
+
+class RouterOptions(C.Structure):
+    _fields_ = [("scoring", C.c_int32), ("renormalize", C.c_int32), ("num_expert_group", C.c_int32),
+                ("topk_group", C.c_int32), ("correction_bias", C.c_void_p), ("routed_scaling_factor", C.c_float)]
 
 
 class EpPeerGroup(C.Structure):
@@ -95,6 +101,12 @@ def load(path: str | None = None):
         L.dsv41_read_status.argtypes = [vp, vp, C.POINTER(C.c_int32)]
         L.dsv41_wait_selftest.restype = C.c_int
         L.dsv41_wait_selftest.argtypes = [vp, C.c_uint32, vp]
+        rp = C.POINTER(RouterOptions)
+        L.dsv41_router_topk.restype = C.c_int
+        L.dsv41_router_topk.argtypes = [vp, i32, i32, i32, i32, rp, i64p, vp, vp]
+        L.dsv41_moe_forward_logits.restype = C.c_int
+        L.dsv41_moe_forward_logits.argtypes = [C.POINTER(MoeLayer), vp, i32, i32, vp, i32, rp, i32,
+                                               C.POINTER(MoeOptions), vp, vp, vp, vp, C.c_size_t, vp]
         gp = C.POINTER(EpPeerGroup)
         L.dsv41_ep_peer_buffer_size.restype = C.c_int
         L.dsv41_ep_peer_buffer_size.argtypes = [gp, C.POINTER(MoeLayer), i32, i32, C.POINTER(C.c_size_t)]

@@ -14,7 +14,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libdsv41_b200.so")
-SOURCES = ["capi.cu", "permute.cu", "transform.cu", "gemv.cu", "gemm.cu", "noalloc.cu", "ep_peer.cu"]
+SOURCES = ["capi.cu", "permute.cu", "transform.cu", "gemv.cu", "gemm.cu", "noalloc.cu", "ep_peer.cu", "router.cu"]
 HEADERS = ["common.cuh", "internal.h", "gemm.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -68,7 +68,7 @@ static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // ------------------------------------------------------------------------------------------
 struct Layout {
     size_t status, counts, offsets, token_sorted, weight_sorted, route_sorted, expert_sorted, route_pos, groups,
-        nlists, fat_experts, seg_hist, xt_g, xt_u, xt_d, y, partials, counters, gemm, total;
+        nlists, fat_experts, seg_hist, xt_g, xt_u, xt_d, y, partials, counters, gemm, r_ids, r_w, total;
     int N, E, H, I, split, groups_bound, units_bound, rows;
 };
 
@@ -124,6 +124,8 @@ static Layout make_layout(int T, int topk, int E, int H, int I, int split_req, i
     L.partials = take(L.split > 1 ? (size_t)L.units_bound * 4096 * 4 : 16);
     L.counters = take((size_t)(L.units_bound / L.split + 1) * 4);
     L.gemm = take(fat >= 0 ? gemm_scratch_bytes(L.rows, E, H, I) : 16);
+    L.r_ids = take(N * 8);   // router output of dsv41_moe_forward_logits
+    L.r_w = take(N * 4);
     L.total = o;
     return L;
 }
@@ -562,6 +564,62 @@ int dsv41_ep_peer_read_status(const dsv41_ep_peer_group* g, const dsv41_moe_laye
     }
     *status = worst;
     return DSV41_OK;
+}
+
+static int check_router(const dsv41_router_options* r, int E, int k)
+{
+    if (!r) return fail(DSV41_E_INVALID, "router options are NULL");
+    if (E <= 0 || E > 1024) return fail(DSV41_E_INVALID, "router supports 1..1024 experts, got %d", E);
+    if (k <= 0 || k > 32 || k > E) return fail(DSV41_E_INVALID, "router topk %d out of range (1..min(32, E))", k);
+    if (r->scoring != DSV41_ROUTER_SOFTMAX && r->scoring != DSV41_ROUTER_SIGMOID)
+        return fail(DSV41_E_INVALID, "bad scoring %d", r->scoring);
+    const int ng = r->num_expert_group;
+    if (ng > 1) {
+        if (ng > 32 || E % ng) return fail(DSV41_E_INVALID, "num_expert_group %d must divide E=%d and be <= 32", ng, E);
+        if (r->topk_group < 1 || r->topk_group > ng)
+            return fail(DSV41_E_INVALID, "topk_group %d out of range 1..%d", r->topk_group, ng);
+        if (k > r->topk_group * (E / ng)) return fail(DSV41_E_INVALID, "topk %d exceeds the competing experts", k);
+    }
+    return DSV41_OK;
+}
+
+int dsv41_router_topk(const void* logits, int32_t logits_dtype, int32_t T, int32_t num_experts, int32_t topk,
+                      const dsv41_router_options* r, int64_t* ids, float* weights, void* stream)
+{
+    int rc = check_router(r, num_experts, topk);
+    if (rc) return rc;
+    if (T < 0 || logits_dtype < DSV41_DTYPE_F16 || logits_dtype > DSV41_DTYPE_F32)
+        return fail(DSV41_E_INVALID, "bad T=%d or logits dtype %d", T, logits_dtype);
+    if (T > 0 && (!logits || !ids || !weights)) return fail(DSV41_E_INVALID, "NULL pointer");
+    cudaError_t err = launch_router_topk(logits, logits_dtype, T, num_experts, topk, r->scoring, r->renormalize,
+                                         r->num_expert_group > 1 ? r->num_expert_group : 1, r->topk_group,
+                                         r->correction_bias, r->routed_scaling_factor, ids, weights,
+                                         static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "router top-k");
+    return DSV41_OK;
+}
+
+int dsv41_moe_forward_logits(const dsv41_moe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
+                             const void* logits, int32_t logits_dtype, const dsv41_router_options* r, int32_t topk,
+                             const dsv41_moe_options* opt, float* out, int64_t* ids_out, float* weights_out,
+                             void* workspace, size_t workspace_bytes, void* stream)
+{
+    int rc = check_layer(layer);
+    if (rc) return rc;
+    if ((rc = check_router(r, layer->num_experts, topk))) return rc;
+    if (!workspace) return fail(DSV41_E_INVALID, "workspace is NULL");
+    const dsv41_moe_options dflt{-1, 0.0f, nullptr, 0, 0, 0};
+    const dsv41_moe_options& o = opt ? *opt : dflt;
+    const int fat = (o.fat_threshold >= 0 && T > o.fat_threshold) ? o.fat_threshold : -1;
+    const Layout L = make_layout(T, topk, layer->num_experts, layer->hidden, layer->intermediate, o.split_k, fat,
+                                 o.max_routes);
+    if (workspace_bytes < L.total)
+        return fail(DSV41_E_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, L.total);
+    if (T == 0) return DSV41_OK;
+    int64_t* ids = ids_out ? ids_out : at<int64_t>(workspace, L.r_ids);
+    float* w = weights_out ? weights_out : at<float>(workspace, L.r_w);
+    if ((rc = dsv41_router_topk(logits, logits_dtype, T, layer->num_experts, topk, r, ids, w, stream))) return rc;
+    return dsv41_moe_forward(layer, x, x_dtype, T, ids, w, topk, opt, out, workspace, workspace_bytes, stream);
 }
 
 size_t dsv41_permute_workspace_size(int32_t T, int32_t topk, int32_t num_experts)

@@ -55,6 +55,9 @@ cudaError_t launch_permute(const int64_t* ids, const float* weights, int N, int 
 cudaError_t launch_prep(const void* x, int x_dtype, const int* token_sorted, const int* expert_sorted,
                         const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
                         cudaStream_t st);
+cudaError_t launch_router_topk(const void* logits, int logits_dtype, int T, int E, int k, int scoring,
+                               int renormalize, int n_group, int topk_group, const float* bias, float scale,
+                               int64_t* ids, float* w, cudaStream_t st);
 cudaError_t launch_prep_rows(const XRows& x, int x_dtype, const int* token_sorted, const int* expert_sorted,
                              const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
                              cudaStream_t st);

@@ -241,6 +241,80 @@ def apply_exl3_fused_moe(x2d: torch.Tensor, ids: torch.Tensor, weights: torch.Te
     return out
 
 
+_SCORING = {"softmax": 0, "sigmoid": 1}
+
+
+def _router_opts(scoring, renormalize, num_expert_group, topk_group, correction_bias, routed_scaling_factor, dev):
+    if scoring not in _SCORING:
+        raise ValueError(f"scoring must be one of {sorted(_SCORING)}")
+    bias = None
+    if correction_bias is not None:
+        bias = correction_bias.to(device=dev, dtype=torch.float32).contiguous()
+    opt = _lib.RouterOptions(_SCORING[scoring], int(bool(renormalize)), int(num_expert_group or 0), int(topk_group or 0),
+                             bias.data_ptr() if bias is not None else None, float(routed_scaling_factor))
+    return opt, bias
+
+
+def route_topk(logits: torch.Tensor, topk: int, *, scoring: str = "softmax", renormalize: bool = True,
+               num_expert_group: int = 0, topk_group: int = 0, correction_bias: torch.Tensor | None = None,
+               routed_scaling_factor: float = 1.0) -> tuple[torch.Tensor, torch.Tensor]:
+    """Router top-k on the GPU (vLLM's routing rule, see dsv41_router_topk): gating logits [T, E]
+    (fp16/bf16/fp32) -> (ids int64 [T, topk], weights fp32 [T, topk]), ids in descending order of
+    their selection value."""
+    L = _lib.load()
+    if logits.dim() != 2 or not logits.is_cuda or logits.dtype not in _DTYPES:
+        raise ValueError("logits must be a CUDA [T, E] fp16/bf16/fp32 tensor")
+    logits = logits.contiguous()
+    T, E = logits.shape
+    dev = logits.device
+    opt, bias = _router_opts(scoring, renormalize, num_expert_group, topk_group, correction_bias,
+                             routed_scaling_factor, dev)
+    ids = torch.empty((T, topk), dtype=torch.int64, device=dev)
+    w = torch.empty((T, topk), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(L.dsv41_router_topk(logits.data_ptr(), _DTYPES[logits.dtype], T, E, topk, C.byref(opt),
+                                       ids.data_ptr(), w.data_ptr(), _stream_ptr(torch.cuda.current_stream(dev))),
+                   "dsv41_router_topk")
+    return ids, w
+
+
+def apply_exl3_fused_moe_logits(x2d: torch.Tensor, logits: torch.Tensor, layer: Exl3MoELayer, topk: int,
+                                limit: float | None = None, *, scoring: str = "softmax", renormalize: bool = True,
+                                num_expert_group: int = 0, topk_group: int = 0,
+                                correction_bias: torch.Tensor | None = None, routed_scaling_factor: float = 1.0,
+                                fat_threshold: int | None = None, return_routes: bool = False):
+    """Router top-k and the routed-expert layer in one C-ABI call (dsv41_moe_forward_logits): the ids
+    and weights go from the router kernel to the permute kernel without leaving the workspace.
+    Returns fp32 [T, H] (and (ids, weights) when return_routes)."""
+    L = _lib.load()
+    layer = as_layer(layer)
+    T, H = x2d.shape
+    dev = layer.device
+    if logits.shape != (T, layer._exl3_num_experts) or logits.dtype not in _DTYPES or x2d.dtype not in _DTYPES:
+        raise ValueError("logits must be [T, E] fp16/bf16/fp32 and x2d fp16/bf16/fp32")
+    x2d, logits = x2d.contiguous(), logits.to(dev).contiguous()
+    ropt, bias = _router_opts(scoring, renormalize, num_expert_group, topk_group, correction_bias,
+                              routed_scaling_factor, dev)
+    fat = FAT_EXPERT_THRESHOLD if fat_threshold is None else int(fat_threshold)
+    lim = float(limit) if (limit is not None and limit > 0) else 0.0
+    opt = _lib.MoeOptions(fat, lim, None, 0, 0, 0)
+    out = torch.empty((T, H), dtype=torch.float32, device=dev)
+    ids = torch.empty((T, topk), dtype=torch.int64, device=dev) if return_routes else None
+    w = torch.empty((T, topk), dtype=torch.float32, device=dev) if return_routes else None
+    stream = torch.cuda.current_stream(dev)
+    nbytes = C.c_size_t()
+    _lib.check(L.dsv41_moe_workspace_size(T, topk, layer._exl3_num_experts, H, layer._exl3_intermediate_local,
+                                          C.byref(opt), C.byref(nbytes)), "workspace_size")
+    ws = _workspace(dev, nbytes.value, stream)
+    with torch.cuda.device(dev):
+        _lib.check(L.dsv41_moe_forward_logits(C.byref(layer._c), x2d.data_ptr(), _DTYPES[x2d.dtype], T,
+                                              logits.data_ptr(), _DTYPES[logits.dtype], C.byref(ropt), topk,
+                                              C.byref(opt), out.data_ptr(), ids.data_ptr() if ids is not None else None,
+                                              w.data_ptr() if w is not None else None, ws.data_ptr(), ws.numel(),
+                                              _stream_ptr(stream)), "dsv41_moe_forward_logits")
+    return (out, (ids, w)) if return_routes else out
+
+
 def apply_exl3_experts(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, layer: Exl3MoELayer,
                        expert_map: torch.Tensor | None = None, limit: float | None = SWIGLU_LIMIT_DEFAULT,
                        **kw) -> torch.Tensor:

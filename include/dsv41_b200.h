@@ -157,6 +157,31 @@ int dsv41_read_status(const void* workspace, void* stream, int32_t* status);
  * Read it with dsv41_read_status; the stream and context stay usable. */
 int dsv41_wait_selftest(void* workspace, uint32_t limit_us, void* stream);
 
+/* Router top-k (no counterpart in the reference: vLLM's FusedMoE router produces topk_ids/weights before
+ * apply_exl3_experts, patches/vllm-exl3-host-dma.patch:496-505). vLLM's two published rules:
+ * scores = softmax(logits) over all experts, or sigmoid(logits); selection = scores (+ correction_bias
+ * when given); with num_expert_group > 1 only the topk_group best groups compete (group score: sum
+ * of its two best selection values with a bias, else its best); ids = top-k selection (ties: lower
+ * id); weights = scores at ids, renormalised to sum 1 if `renormalize`, times routed_scaling_factor.
+ * E <= 1024, topk <= 32. dsv41_moe_forward_logits = router + dsv41_moe_forward in one call (ids and
+ * weights stay in the workspace unless ids_out/weights_out are given). */
+enum { DSV41_ROUTER_SOFTMAX = 0, DSV41_ROUTER_SIGMOID = 1 };
+typedef struct dsv41_router_options {
+    int32_t scoring;                /* DSV41_ROUTER_SOFTMAX or DSV41_ROUTER_SIGMOID */
+    int32_t renormalize;            /* nonzero: weights / sum(weights) over the k chosen */
+    int32_t num_expert_group;       /* 0 or 1 = no grouping */
+    int32_t topk_group;
+    const float* correction_bias;   /* device [E] fp32 or NULL */
+    float routed_scaling_factor;    /* 1.0 = none */
+} dsv41_router_options;
+
+int dsv41_router_topk(const void* logits, int32_t logits_dtype, int32_t T, int32_t num_experts, int32_t topk,
+                      const dsv41_router_options* router, int64_t* ids, float* weights, void* stream);
+int dsv41_moe_forward_logits(const dsv41_moe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
+                             const void* logits, int32_t logits_dtype, const dsv41_router_options* router, int32_t topk,
+                             const dsv41_moe_options* opt, float* out, int64_t* ids_out, float* weights_out,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * Expert parallelism over NVLink peer memory (no counterpart in the reference, which runs one GPU
  * with experts in host RAM, docker/entrypoint.sh:135-140). Experts are sharded: global expert e

@@ -102,3 +102,20 @@ def test_oracle_against_local_reference_build(oracle):
     for _ in range(64):
         tile = rng.integers(0, 65536, 48, dtype=np.uint16)
         assert np.array_equal(oracle.states(tile), ref.states(tile))
+
+
+def test_router_oracle_matches_vllm_golden():
+    """The numpy router restatement reproduces vLLM's own routing (golden vectors from its torch
+    grouped_topk: softmax top-k, sigmoid + correction bias with groups, grouped max, grouped softmax)."""
+    from oracle.router import router_topk
+    g = golden("router.npz")
+    names = sorted(set(k.split("__")[0] for k in g.files))
+    assert len(names) == 4
+    for n in names:
+        T, E, k, sig, renorm, ng, tg, wb, scale = g[n + "__cfg"]
+        ids, w = router_topk(g[n + "__logits"], int(k), "sigmoid" if sig else "softmax", bool(renorm), int(ng),
+                             int(tg), g[n + "__bias"] if wb else None, float(scale))
+        for a, wa, b, wbv in zip(ids, w, g[n + "__ids"], g[n + "__w"]):
+            assert set(a.tolist()) == set(b.tolist()), n
+            ref = dict(zip(b.tolist(), wbv.tolist()))
+            assert max(abs(x - ref[i]) for i, x in zip(a.tolist(), wa.tolist())) < 1e-6, n
