@@ -19,7 +19,7 @@ OK, E_INVALID, E_CUDA, E_WORKSPACE = 0, -1, -2, -3
 SYMBOLS = (
     "dsv41_last_error", "dsv41_abi_version", "dsv41_build_info", "dsv41_moe_workspace_size",
     "dsv41_moe_forward", "dsv41_moe_forward_noalloc", "dsv41_permute_workspace_size", "dsv41_permute", "dsv41_combine",
-    "dsv41_decode_dense", "dsv41_expert_gemm", "dsv41_expert_gemm_workspace_size", "dsv41_read_status", "dsv41_wait_selftest",
+    "dsv41_decode_dense", "dsv41_decode_dense_bits", "dsv41_expert_gemm", "dsv41_expert_gemm_workspace_size", "dsv41_read_status", "dsv41_wait_selftest",
     "dsv41_router_topk", "dsv41_moe_forward_logits",
     "dsv41_ep_peer_buffer_size", "dsv41_ep_peer_alloc", "dsv41_ep_peer_open", "dsv41_ep_peer_close", "dsv41_ep_peer_free",
     "dsv41_ep_peer_forward", "dsv41_ep_peer_read_status",
@@ -33,7 +33,7 @@ STAGE_NAMES = ("permute", "prep", "gemv_gateup", "gemm_gateup", "gemv_down", "ge
 
 class MoeLayer(C.Structure):
     _fields_ = [("num_experts", C.c_int32), ("hidden", C.c_int32), ("intermediate", C.c_int32),
-                ("reserved", C.c_int32), ("gate_ptrs", C.c_void_p), ("up_ptrs", C.c_void_p),
+                ("bits", C.c_int32), ("gate_ptrs", C.c_void_p), ("up_ptrs", C.c_void_p),
                 ("down_ptrs", C.c_void_p), ("w13_suh", C.c_void_p), ("w13_svh", C.c_void_p),
                 ("w2_suh", C.c_void_p), ("w2_svh", C.c_void_p)]
 
@@ -92,6 +92,8 @@ def load(path: str | None = None):
         L.dsv41_combine.argtypes = [vp, vp, vp, i32, i32, i32, i32, vp, vp]
         L.dsv41_decode_dense.restype = C.c_int
         L.dsv41_decode_dense.argtypes = [vp, i32, i32, vp, vp]
+        L.dsv41_decode_dense_bits.restype = C.c_int
+        L.dsv41_decode_dense_bits.argtypes = [vp, i32, i32, i32, vp, vp]
         L.dsv41_expert_gemm.restype = C.c_int
         L.dsv41_expert_gemm.argtypes = [C.POINTER(MoeLayer), vp, i32, i32, vp, i32, vp, vp, vp, vp, i32, C.c_float, vp,
                                         vp, C.c_size_t, vp]

@@ -210,6 +210,8 @@ static int check_group(const dsv41_ep_peer_group* g)
 // decode GEMV (the reference's FAT_EXPERT_THRESHOLD as deployed, docker/entrypoint.sh:69)
 constexpr int kExpertGemmFat = 32;
 
+static int layer_bits(const dsv41_moe_layer* layer) { return layer->bits ? layer->bits : 3; }
+
 static int check_layer(const dsv41_moe_layer* layer)
 {
     if (!layer) return fail(DSV41_E_INVALID, "layer is NULL");
@@ -220,6 +222,8 @@ static int check_layer(const dsv41_moe_layer* layer)
     if (!layer->gate_ptrs || !layer->up_ptrs || !layer->down_ptrs || !layer->w13_suh || !layer->w13_svh ||
         !layer->w2_suh || !layer->w2_svh)
         return fail(DSV41_E_INVALID, "layer has a NULL tensor pointer");
+    if (layer->bits != 0 && (layer->bits < 2 || layer->bits > 4))
+        return fail(DSV41_E_INVALID, "bits %d per weight (2, 3 or 4)", layer->bits);
     return DSV41_OK;
 }
 
@@ -288,6 +292,7 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
     ga.scratch = gemm_scratch;
     ga.status = status;
     GemvParams gp{};
+    gp.bits = layer_bits(layer);
     gp.groups = pb.groups;
     gp.n_groups = pb.n_groups;
     gp.partials = partials;
@@ -686,14 +691,21 @@ int dsv41_combine(const void* y, const int32_t* route_pos, const float* weights,
     return DSV41_OK;
 }
 
-int dsv41_decode_dense(const void* trellis, int32_t k, int32_t n, void* w_out, void* stream)
+int dsv41_decode_dense_bits(const void* trellis, int32_t k, int32_t n, int32_t bits, void* w_out, void* stream)
 {
     if (k <= 0 || n <= 0 || k % 16 || n % 16) return fail(DSV41_E_INVALID, "k=%d n=%d must be multiples of 16", k, n);
+    if (bits < 2 || bits > 4) return fail(DSV41_E_INVALID, "bits %d (2, 3 or 4)", bits);
     if (!trellis || !w_out) return fail(DSV41_E_INVALID, "NULL pointer");
     if (reinterpret_cast<uintptr_t>(trellis) % 4) return fail(DSV41_E_INVALID, "trellis must be 4-byte aligned");
-    cudaError_t err = launch_decode_dense(trellis, k, n, static_cast<__half*>(w_out), static_cast<cudaStream_t>(stream));
+    cudaError_t err =
+        launch_decode_dense(trellis, k, n, bits, static_cast<__half*>(w_out), static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(err, "decode_dense");
     return DSV41_OK;
+}
+
+int dsv41_decode_dense(const void* trellis, int32_t k, int32_t n, void* w_out, void* stream)
+{
+    return dsv41_decode_dense_bits(trellis, k, n, 3, w_out, stream);
 }
 
 static size_t expert_gemm_layout(int R, int n_experts, int H, int I, size_t* offs)

@@ -28,26 +28,6 @@ enum : int { kStatusOk = 0, kStatusWaitTimeout = 1, kStatusBadShape = 2, kStatus
 // ------------------------------------------------------------------------------------------
 // decode
 // ------------------------------------------------------------------------------------------
-struct LaneDecode {
-    int w_hi, w_lo;  // word indices of this lane's 64-bit window inside the tile
-    uint32_t pre;    // pre-shift (0 or 16) that brings every state below bit 32 of the window
-    int base;        // shift of symbol 0; symbol j is at base - 3j
-};
-
-// Lane t's 8 states span stream bits [24t-13, 24t+24). With o = start % 32 that window fits in
-// words (a, a+1); lanes with o < 16 shift the pair right by 16 first so all 8 shifts are < 32.
-__device__ __forceinline__ LaneDecode lane_decode_setup(int t)
-{
-    const int start = (24 * t - 13 + 768) % 768;
-    const int a = start >> 5, o = start & 31;
-    LaneDecode d;
-    d.w_hi = a;
-    d.w_lo = (a + 1) % kTileWords;
-    if (o < 16) { d.pre = 16; d.base = 32 - o; }
-    else { d.pre = 0; d.base = 48 - o; }
-    return d;
-}
-
 __device__ __forceinline__ __half2 u32_as_half2(uint32_t v)
 {
     __half2 h;
@@ -60,24 +40,6 @@ __device__ __forceinline__ uint32_t half2_as_u32(__half2 h) { return *reinterpre
 __device__ __forceinline__ uint32_t state_code(uint32_t st)
 {
     return __dp4a(st * kMul1, 0x01010101u, 0x6400u);
-}
-
-// Decode this lane's 8 symbols of one tile (its two window words) into 4 half2 registers in
-// mma B-fragment order: b[0] = (k r0, r0+1 | n c0), b[1] = (r0+8, r0+9 | c0), b[2], b[3] same
-// for column c0+8. One fp16 rounding per weight (HFMA2), bit-exact with the reference decode.
-__device__ __forceinline__ void decode_lane(uint32_t whi, uint32_t wlo, const LaneDecode& d, uint32_t (&b)[4])
-{
-    const uint32_t lo = __funnelshift_r(wlo, whi, d.pre);
-    const uint32_t hi = whi >> d.pre;
-    const __half2 kinv = u32_as_half2((uint32_t)kKinvBits * 0x10001u);
-    const __half2 kbias = u32_as_half2((uint32_t)kKbiasBits * 0x10001u);
-#pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-        const uint32_t s0 = __funnelshift_r(lo, hi, d.base - 3 * j) & 0xffffu;
-        const uint32_t s1 = __funnelshift_r(lo, hi, d.base - 3 * (j + 1)) & 0xffffu;
-        const uint32_t c = __byte_perm(state_code(s0), state_code(s1), 0x5410);
-        b[j >> 1] = half2_as_u32(__hfma2(u32_as_half2(c), kinv, kbias));
-    }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -127,6 +89,74 @@ __device__ __forceinline__ void decode_lane_u(uint32_t w0, uint32_t w1, uint32_t
         const uint32_t c0 = state_code(s[j]), c1 = state_code(s[j + 1]);
         const uint32_t c = (j == 0) ? c1 * k16 + c0 : __byte_perm(c0, c1, 0x5410);
         b[j >> 1] = half2_as_u32(__hfma2(u32_as_half2(c), kinv, kbias));
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Bits per weight K = 2, 3, 4. A tile is 16*K int16 words = 32*K bytes, a circular 256*K-bit stream
+// whose symbol i state is the 16-bit window ending at stream bit K*i+K-1 (the reference's
+// BITS-generic state_scalar, ft_core.h:63-73). K = 3 uses the lane-uniform window above; for
+// K = 4 and 2 lane t's 8 states lie in two consecutive 32-bit words (a, b):
+//   K = 4: a = t-1, b = t (mod 32); state j = bits [28-4j, 44-4j) of (word a : word b)
+//   K = 2: a = t/2-1, b = t/2 (mod 16); state j = bits [s0-2j, s0-2j+16), s0 = 30 (even t) or
+//          14 (odd t)
+// so every state is one funnel shift (by less than 32) and a 16-bit mask.
+// ------------------------------------------------------------------------------------------
+template <int K>
+struct TileFmt {
+    static_assert(K == 2 || K == 3 || K == 4, "2, 3 or 4 bits per weight");
+    static constexpr int bytes = 32 * K;
+    static constexpr int words = 8 * K;
+};
+
+template <int K>
+struct LaneDec {
+    int q0, q1, q2;
+    uint32_t r;   // K = 3: left funnel shift of the window; K = 2, 4: shift of state 0
+};
+
+template <int K>
+__device__ __forceinline__ LaneDec<K> lane_dec_setup(int t)
+{
+    LaneDec<K> d;
+    if constexpr (K == 3) {
+        const LaneWindow w = lane_window_setup(t);
+        d.q0 = w.q0;
+        d.q1 = w.q1;
+        d.q2 = w.q2;
+        d.r = w.r8;
+    } else if constexpr (K == 4) {
+        d.q0 = (t + 31) & 31;
+        d.q1 = t;
+        d.q2 = 0;
+        d.r = 28;
+    } else {
+        d.q0 = ((t >> 1) + 15) & 15;
+        d.q1 = t >> 1;
+        d.q2 = 0;
+        d.r = (t & 1) ? 14u : 30u;
+    }
+    return d;
+}
+
+// this lane's 8 weights of the tile at `tw` as 4 half2 mma B-fragment registers (bit-exact)
+template <int K>
+__device__ __forceinline__ void decode_tile(const uint32_t* tw, const LaneDec<K>& d, uint32_t k16, uint32_t (&b)[4])
+{
+    if constexpr (K == 3) {
+        decode_lane_u(tw[d.q0], tw[d.q1], tw[d.q2], d.r, k16, b);
+    } else {
+        const uint32_t hi = tw[d.q0], lo = tw[d.q1];
+        const __half2 kinv = u32_as_half2((uint32_t)kKinvBits * 0x10001u);
+        const __half2 kbias = u32_as_half2((uint32_t)kKbiasBits * 0x10001u);
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+            const uint32_t s0 = __funnelshift_r(lo, hi, d.r - K * j) & 0xffffu;
+            const uint32_t s1 = __funnelshift_r(lo, hi, d.r - K * (j + 1)) & 0xffffu;
+            const uint32_t c0 = state_code(s0), c1 = state_code(s1);
+            const uint32_t c = (j == 0) ? c1 * k16 + c0 : __byte_perm(c0, c1, 0x5410);
+            b[j >> 1] = half2_as_u32(__hfma2(u32_as_half2(c), kinv, kbias));
+        }
     }
 }
 

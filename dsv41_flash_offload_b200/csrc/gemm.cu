@@ -60,21 +60,22 @@ constexpr int kRowB = kBK * 2;          // bytes of one operand row in a stage (
 constexpr int kAtom = 8 * kRowB;        // bytes of one 8-row swizzle atom
 constexpr int kTileA = kBM * kRowB;     // one 128-row activation tile
 constexpr int kTileB = kBN * kRowB;     // one 128-feature decoded weight tile
-constexpr int kTrRow = 8 * kTileBytes;  // 768 B: 8 n-tiles of one k-tile row
+template <int K>
+__host__ __device__ constexpr int tr_row() { return 8 * TileFmt<K>::bytes; }   // 8 n-tiles of one k-tile row (768 B at K = 3)
 
 // Three independent rings per CTA (each with full/empty mbarriers):
 //   A (activations, TMA)   released by tcgen05.commit after the chunk's MMAs
 //   B (decoded weights)    written by the decoders, released by tcgen05.commit
 //   T (trellis k-rows)     filled by the trellis producer, released by the decoders, so the
 //                          compressed words stream ahead of the MMAs by several chunks
-template <int MODE>
+template <int MODE, int K>
 struct GemmCfg {
     static constexpr int nmat = MODE == 0 ? 2 : 1;
     static constexpr int mtiles = MODE == 0 ? 2 : 4;      // M tiles per pass
     static constexpr int rows_per_pass = mtiles * kBM;
     static constexpr int a_bytes = nmat * mtiles * kTileA;
     static constexpr int b_bytes = nmat * kTileB;
-    static constexpr int t_bytes = nmat * kKT * kTrRow;
+    static constexpr int t_bytes = nmat * kKT * tr_row<K>();
     static constexpr int a_stages = 2 * (64 / kBK);
     static constexpr int b_stages = (MODE == 0 ? 2 : 3) * (64 / kBK);
     static constexpr int t_stages = (MODE == 0 ? 4 : 8) * (64 / kBK);
@@ -224,10 +225,11 @@ __device__ __forceinline__ void out_block128(float (&v)[128], const __half* svh)
 // ---------------------------------------------------------------------------------------------
 // kernel
 // ---------------------------------------------------------------------------------------------
-template <int MODE>
+template <int MODE, int K>
 __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid_constant__ GemmParams p)
 {
-    using Cfg = GemmCfg<MODE>;
+    using Cfg = GemmCfg<MODE, K>;
+    constexpr int kTrRow = tr_row<K>();
     constexpr int AS = Cfg::a_stages, BS = Cfg::b_stages, TS = Cfg::t_stages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
@@ -320,7 +322,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
             if (lane >= Cfg::nmat * kKT || u >= n_units) return nullptr;
             const int e = p.passes[u / n_fb].x, fb = u % n_fb;
             const int64_t base = (lane / kKT) ? p.tab_b[e] : p.tab_a[e];
-            return reinterpret_cast<const uint8_t*>(base) + ((size_t)(c * kKT + lane % kKT) * ntile_row + fb * 8) * kTileBytes;
+            return reinterpret_cast<const uint8_t*>(base) + ((size_t)(c * kKT + lane % kKT) * ntile_row + fb * 8) * TileFmt<K>::bytes;
         };
         // L2 prefetch runs kTrPrefetch chunks ahead of the copies (into the next unit near the end),
         // so the ring's copies see L2 latency rather than HBM latency
@@ -347,7 +349,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 __syncwarp();
                 if (lane < Cfg::nmat * kKT) {
                     const int mat = lane / kKT, kt = lane % kKT;
-                    const uint8_t* src = tr[mat] + ((size_t)(c * kKT + kt) * ntile_row + fb * 8) * kTileBytes;
+                    const uint8_t* src = tr[mat] + ((size_t)(c * kKT + kt) * ntile_row + fb * 8) * TileFmt<K>::bytes;
                     bulk_g2s(stage_t(s, mat, kt), src, kTrRow, &t_full[s], pol);
                 }
             }
@@ -413,7 +415,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
     } else if (warp >= kWarpDec0) {
         // ------------------------------- decoders + epilogue -------------------------------
         const int d = warp - kWarpDec0;               // 0..7
-        const LaneWindow lw = lane_window_setup(lane);
+        const LaneDec<K> lw = lane_dec_setup<K>(lane);
         const uint32_t k16 = p.k16;
         const int r0 = (lane & 3) * 2, c0 = lane >> 2;
         // decode assignment: the chunk's nmat * kKT (matrix, k-tile) rows of 8 n-tiles are split
@@ -452,9 +454,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 uint8_t* bt = stage_b(sb, dmat) + nt0 * 2 * kAtom;
 #pragma unroll kDecUnroll
                 for (int j = 0; j < ntn; ++j) {
-                    const uint32_t* tw = trw + (nt0 + j) * kTileWords;
+                    const uint32_t* tw = trw + (nt0 + j) * TileFmt<K>::words;
                     uint32_t b[4];
-                    decode_lane_u(tw[lw.q0], tw[lw.q1], tw[lw.q2], lw.r8, k16, b);
+                    decode_tile<K>(tw, lw, k16, b);
 #pragma unroll
                     for (int q = 0; q < 4; ++q) *reinterpret_cast<uint32_t*>(bt + j * 2 * kAtom + boff[q]) = b[q];
                 }
@@ -574,10 +576,10 @@ __global__ void gemm_plan_kernel(const int* fat_experts, const int* n_fat, const
     int a = 0, b = 0;
     for (int i = 0; i < nf; ++i) {
         const int e = fat_experts[i], R = counts[e], r0 = offsets[e];
-        for (int r = 0; r < R; r += GemmCfg<0>::rows_per_pass)
-            passes0[a++] = make_int4(e, r0 + r, min(GemmCfg<0>::rows_per_pass, R - r), 0);
-        for (int r = 0; r < R; r += GemmCfg<1>::rows_per_pass)
-            passes1[b++] = make_int4(e, r0 + r, min(GemmCfg<1>::rows_per_pass, R - r), 0);
+        for (int r = 0; r < R; r += GemmCfg<0, 3>::rows_per_pass)
+            passes0[a++] = make_int4(e, r0 + r, min(GemmCfg<0, 3>::rows_per_pass, R - r), 0);
+        for (int r = 0; r < R; r += GemmCfg<1, 3>::rows_per_pass)
+            passes1[b++] = make_int4(e, r0 + r, min(GemmCfg<1, 3>::rows_per_pass, R - r), 0);
     }
     *n0 = a;
     *n1 = b;
@@ -588,7 +590,7 @@ static int max_passes(int N, int /*E*/, int rp) { return N / rp + (N < kMaxExper
 
 size_t gemm_scratch_bytes(int N, int E, int H, int I)
 {
-    return (size_t)(max_passes(N, E, GemmCfg<0>::rows_per_pass) + max_passes(N, E, GemmCfg<1>::rows_per_pass)) * 16 + 256;
+    return (size_t)(max_passes(N, E, GemmCfg<0, 3>::rows_per_pass) + max_passes(N, E, GemmCfg<1, 3>::rows_per_pass)) * 16 + 256;
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
@@ -620,14 +622,14 @@ static cudaError_t make_map(CUtensorMap* m, const void* base, int rows, int K)
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int MODE>
+template <int MODE, int K>
 static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
 {
-    using Cfg = GemmCfg<MODE>;
+    using Cfg = GemmCfg<MODE, K>;
     const int H = a.layer->hidden, I = a.layer->intermediate, E = a.layer->num_experts;
     const int N = a.rows_bound;
     int4* passes0 = reinterpret_cast<int4*>(a.scratch + 256);
-    int4* passes1 = passes0 + max_passes(N, E, GemmCfg<0>::rows_per_pass);
+    int4* passes1 = passes0 + max_passes(N, E, GemmCfg<0, 3>::rows_per_pass);
     int* counters = reinterpret_cast<int*>(a.scratch);
     cudaError_t err;
     if (MODE == 0) {
@@ -665,18 +667,28 @@ static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
     p.limit = a.limit;
     p.k16 = 65536u;
     const size_t smem = Cfg::smem_bytes;
-    if ((err = cudaFuncSetAttribute((const void*)exl3_gemm_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if ((err = cudaFuncSetAttribute((const void*)exl3_gemm_kernel<MODE, K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)smem)) != cudaSuccess)
         return err;
     const int units_bound = max_passes(N, E, Cfg::rows_per_pass) * (p.N / kBN);
     int grid = num_sms();
     if (units_bound < grid) grid = units_bound;
     if (grid < 1) grid = 1;
-    exl3_gemm_kernel<MODE><<<grid, kGemmThreads, smem, st>>>(p);
+    exl3_gemm_kernel<MODE, K><<<grid, kGemmThreads, smem, st>>>(p);
     return cudaGetLastError();
 }
 
-cudaError_t launch_gemm_gateup(const GemmArgs& a, cudaStream_t st) { return launch_mode<0>(a, st); }
-cudaError_t launch_gemm_down(const GemmArgs& a, cudaStream_t st) { return launch_mode<1>(a, st); }
+static int args_bits(const GemmArgs& a) { return a.layer->bits ? a.layer->bits : 3; }
+
+cudaError_t launch_gemm_gateup(const GemmArgs& a, cudaStream_t st)
+{
+    const int b = args_bits(a);
+    return b == 2 ? launch_mode<0, 2>(a, st) : b == 4 ? launch_mode<0, 4>(a, st) : launch_mode<0, 3>(a, st);
+}
+cudaError_t launch_gemm_down(const GemmArgs& a, cudaStream_t st)
+{
+    const int b = args_bits(a);
+    return b == 2 ? launch_mode<1, 2>(a, st) : b == 4 ? launch_mode<1, 4>(a, st) : launch_mode<1, 3>(a, st);
+}
 
 }  // namespace dsv41

@@ -9,7 +9,7 @@
 //
 // Work unit = (row group of <= 16 rows of one expert, column block, K split). A persistent grid
 // of 2 CTAs per SM walks the units. Per CTA: 8 consumer warps + 1 producer warp.
-//   producer: one 1-D bulk async copy (cp.async.bulk, into this CTA only) per 768/1536-byte trellis
+//   producer: one 1-D bulk async copy (cp.async.bulk, into this CTA only) per 8/16-tile trellis
 //             k-row segment and per 256-byte activation row into a 2-stage mbarrier ring of 16
 //             k-rows per stage; trellis reads carry an L2 evict-first hint (each expert byte is
 //             read once).
@@ -46,13 +46,15 @@ constexpr int kConsumerWarps = 16 / kTilesPerWarp;   // 16 n-tiles per staged k-
 constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
 constexpr int kStageRows = DSV41_GEMV_STAGE_ROWS;
 constexpr int kStages = DSV41_GEMV_STAGES;
-constexpr int kRowBytes = 1536;        // 16 tiles of one k-row
+template <int K>
+__host__ __device__ constexpr int row_bytes() { return 16 * TileFmt<K>::bytes; }   // 16 tiles of one k-row (1536 B at K = 3)
 constexpr int kXRowStride = kStageRows * 32 + 16;  // stage's k-tiles x 16 halves, + 16 B pad (ldmatrix banks)
 constexpr int kXMatBytes = 16 * kXRowStride;
 constexpr int kEpFloats = 4096;
 
+template <int K>
 struct GemvSmem {
-    uint8_t tr[kStages][kStageRows * kRowBytes];
+    uint8_t tr[kStages][kStageRows * row_bytes<K>()];
     uint8_t x[kStages][2][kXMatBytes];
     float ep[kEpFloats];
     uint64_t full[kStages];
@@ -61,7 +63,10 @@ struct GemvSmem {
     int last_flag;
 };
 
-size_t gemv_smem_bytes() { return sizeof(GemvSmem); }
+size_t gemv_smem_bytes(int bits)
+{
+    return bits == 2 ? sizeof(GemvSmem<2>) : bits == 4 ? sizeof(GemvSmem<4>) : sizeof(GemvSmem<3>);
+}
 int gemv_stage_rows() { return kStageRows; }
 
 __device__ __forceinline__ void out_block4(float (&y)[4], const __half* svh, int lane)
@@ -76,11 +81,12 @@ __device__ __forceinline__ void out_block4(float (&y)[4], const __half* svh, int
     for (int q = 0; q < 4; ++q) y[q] = r16(__fmul_rn(__fmul_rn(y[q], kHad), s[q]));
 }
 
-template <int MODE>
+template <int MODE, int K>
 __global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv_kernel(const GemvParams p)
 {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    GemvSmem& S = *reinterpret_cast<GemvSmem*>(smem_raw);
+    GemvSmem<K>& S = *reinterpret_cast<GemvSmem<K>*>(smem_raw);
+    constexpr int kTB = TileFmt<K>::bytes, kTW = TileFmt<K>::words, kRowBytes = row_bytes<K>();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int nmat = MODE == 0 ? 2 : 1;
     constexpr int cols = MODE == 0 ? 128 : 256;
@@ -127,12 +133,12 @@ __global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv
                 if (MODE == 0) {
                     if (lane < 2 * kStageRows) {
                         const int r = lane >> 1, which = lane & 1;
-                        const uint8_t* src = (which ? tb : ta) + ((size_t)(kt0 + r) * ntile_row + cb * 8) * kTileBytes;
-                        bulk_g2s(S.tr[stage] + r * kRowBytes + which * 768, src, 768, &S.full[stage], pol_w);
+                        const uint8_t* src = (which ? tb : ta) + ((size_t)(kt0 + r) * ntile_row + cb * 8) * kTB;
+                        bulk_g2s(S.tr[stage] + r * kRowBytes + which * 8 * kTB, src, 8 * kTB, &S.full[stage], pol_w);
                     }
                 } else {
                     if (lane < kStageRows) {
-                        const uint8_t* src = ta + ((size_t)(kt0 + lane) * ntile_row + cb * 16) * kTileBytes;
+                        const uint8_t* src = ta + ((size_t)(kt0 + lane) * ntile_row + cb * 16) * kTB;
                         bulk_g2s(S.tr[stage] + lane * kRowBytes, src, kRowBytes, &S.full[stage], pol_w);
                     }
                 }
@@ -156,7 +162,7 @@ __global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv
     }
 
     // ------------------------------ consumer warps ------------------------------
-    const LaneWindow lw = lane_window_setup(lane);
+    const LaneDec<K> lw = lane_dec_setup<K>(lane);
     const uint32_t k16 = p.k16;
     const int tile0 = warp * kTilesPerWarp;       // first of this warp's adjacent n-tiles (0..15)
     const int mat = MODE == 0 ? (tile0 >> 3) : 0;  // gate/up pass: tiles 0-7 gate, 8-15 up
@@ -177,8 +183,8 @@ __global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv
             const int stage = it % kStages;
             const uint32_t round = it / kStages;
             mbar_wait_bounded(&S.full[stage], round & 1, &S.abort_flag, p.status);
-            // this warp's tiles sit at byte offset tile * 96 of each staged 1536-byte k-row
-            const uint32_t* trow = reinterpret_cast<const uint32_t*>(S.tr[stage]) + tile0 * kTileWords;
+            // this warp's tiles sit at byte offset tile * 32K of each staged 16-tile k-row
+            const uint32_t* trow = reinterpret_cast<const uint32_t*>(S.tr[stage]) + tile0 * kTW;
             const uint32_t xaddr = smem_addr(S.x[stage][mat]) + x_lane;
 #pragma unroll
             for (int r = 0; r < kStageRows; ++r) {
@@ -186,9 +192,9 @@ __global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv
                 ldmatrix_x4(a, xaddr + r * 32);
 #pragma unroll
                 for (int t = 0; t < kTilesPerWarp; ++t) {
-                    const uint32_t* tw = trow + r * (kRowBytes / 4) + t * kTileWords;
+                    const uint32_t* tw = trow + r * (kRowBytes / 4) + t * kTW;
                     uint32_t b[4];
-                    decode_lane_u(tw[lw.q0], tw[lw.q1], tw[lw.q2], lw.r8, k16, b);
+                    decode_tile<K>(tw, lw, k16, b);
                     mma_16816(acc[t][0], a, b[0], b[1]);
                     mma_16816(acc[t][1], a, b[2], b[3]);
                 }
@@ -292,20 +298,25 @@ int gemv_units_alloc(int groups_bound, int H, int I, int split)
     return groups_bound * cb * split;
 }
 
-cudaError_t launch_gemv(int mode, const GemvParams& p, int units_bound, cudaStream_t st)
+template <int MODE, int K>
+static cudaError_t launch_gemv_k(const GemvParams& p, int units_bound, cudaStream_t st)
 {
-    const size_t smem = sizeof(GemvSmem);
-    const void* fn = mode == 0 ? (const void*)exl3_gemv_kernel<0> : (const void*)exl3_gemv_kernel<1>;
-    cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const size_t smem = sizeof(GemvSmem<K>);
+    cudaError_t err = cudaFuncSetAttribute((const void*)exl3_gemv_kernel<MODE, K>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
     int grid = DSV41_GEMV_MIN_BLOCKS * num_sms();
     if (units_bound < grid) grid = units_bound;
     if (grid < 1) grid = 1;
-    if (mode == 0)
-        exl3_gemv_kernel<0><<<grid, kGemvThreads, smem, st>>>(p);
-    else
-        exl3_gemv_kernel<1><<<grid, kGemvThreads, smem, st>>>(p);
+    exl3_gemv_kernel<MODE, K><<<grid, kGemvThreads, smem, st>>>(p);
     return cudaGetLastError();
+}
+
+cudaError_t launch_gemv(int mode, const GemvParams& p, int units_bound, cudaStream_t st)
+{
+    if (p.bits == 2) return mode == 0 ? launch_gemv_k<0, 2>(p, units_bound, st) : launch_gemv_k<1, 2>(p, units_bound, st);
+    if (p.bits == 4) return mode == 0 ? launch_gemv_k<0, 4>(p, units_bound, st) : launch_gemv_k<1, 4>(p, units_bound, st);
+    return mode == 0 ? launch_gemv_k<0, 3>(p, units_bound, st) : launch_gemv_k<1, 3>(p, units_bound, st);
 }
 
 }  // namespace dsv41

@@ -80,6 +80,7 @@ cudaError_t launch_list_setup(const int32_t* experts, int n_experts, const int64
                               int* nrows, cudaStream_t st);
 
 struct GemvParams {
+    int bits;              // bits per weight K of the trellis (2, 3, 4)
     const int4* groups;
     const int* n_groups;
     const int64_t* tab_a;  // gate (gate/up pass) or down trellis addresses [E]
@@ -99,7 +100,7 @@ struct GemvParams {
 
 int gemv_units_bound(int groups_bound, int K, int N, int mode, int split);
 int gemv_units_alloc(int groups_bound, int H, int I, int split);
-size_t gemv_smem_bytes();
+size_t gemv_smem_bytes(int bits);
 int gemv_stage_rows();   // k-tile rows per pipeline stage: a K split must be a multiple of it
 cudaError_t launch_gemv(int mode, const GemvParams& p, int units_bound, cudaStream_t st);
 
@@ -110,7 +111,7 @@ cudaError_t launch_scatter_add(const __half* y, const int* expert_list, int n_li
                                const float* weight_sorted, int H, int rows_bound, float* out,
                                cudaStream_t st);
 
-cudaError_t launch_decode_dense(const void* trellis, int k, int n, __half* w, cudaStream_t st);
+cudaError_t launch_decode_dense(const void* trellis, int k, int n, int bits, __half* w, cudaStream_t st);
 cudaError_t launch_wait_selftest(int* status, uint64_t limit_ns, cudaStream_t st);
 
 int num_sms();

@@ -162,18 +162,19 @@ cudaError_t launch_scatter_add(const __half* y, const int* expert_list, int n_li
 }
 
 // one warp per 16x16 tile
+template <int K>
 __global__ void __launch_bounds__(256) decode_dense_kernel(const uint32_t* trellis, int k, int n, __half* w)
 {
     const int lane = threadIdx.x & 31;
     const int tn_count = n / 16;
     const long long tiles = (long long)(k / 16) * tn_count;
-    const LaneDecode ld = lane_decode_setup(lane);
+    const LaneDec<K> ld = lane_dec_setup<K>(lane);
     const int r0 = (lane % 4) * 2, c0 = lane / 4;
     for (long long tile = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tile < tiles;
          tile += (long long)gridDim.x * (blockDim.x >> 5)) {
-        const uint32_t* tw = trellis + tile * kTileWords;
+        const uint32_t* tw = trellis + tile * TileFmt<K>::words;
         uint32_t b[4];
-        decode_lane(__ldg(tw + ld.w_hi), __ldg(tw + ld.w_lo), ld, b);
+        decode_tile<K>(tw, ld, 65536u, b);
         const int tk = (int)(tile / tn_count), tn = (int)(tile % tn_count);
         __half* base = w + (size_t)(tk * 16) * n + tn * 16;
         const int rows[4] = {r0, r0 + 8, r0, r0 + 8};
@@ -187,14 +188,17 @@ __global__ void __launch_bounds__(256) decode_dense_kernel(const uint32_t* trell
     }
 }
 
-cudaError_t launch_decode_dense(const void* trellis, int k, int n, __half* w, cudaStream_t st)
+cudaError_t launch_decode_dense(const void* trellis, int k, int n, int bits, __half* w, cudaStream_t st)
 {
     const long long tiles = (long long)(k / 16) * (n / 16);
     long long blocks = (tiles + 7) / 8;
     const long long cap = (long long)num_sms() * 16;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    decode_dense_kernel<<<(int)blocks, 256, 0, st>>>(static_cast<const uint32_t*>(trellis), k, n, w);
+    const uint32_t* t = static_cast<const uint32_t*>(trellis);
+    if (bits == 2) decode_dense_kernel<2><<<(int)blocks, 256, 0, st>>>(t, k, n, w);
+    else if (bits == 4) decode_dense_kernel<4><<<(int)blocks, 256, 0, st>>>(t, k, n, w);
+    else decode_dense_kernel<3><<<(int)blocks, 256, 0, st>>>(t, k, n, w);
     return cudaGetLastError();
 }
 

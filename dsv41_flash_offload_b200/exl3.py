@@ -57,10 +57,11 @@ class Exl3MoELayer:
     def __init__(self, w13_trellis: torch.Tensor, w2_trellis: torch.Tensor, w13_suh: torch.Tensor,
                  w13_svh: torch.Tensor, w2_suh: torch.Tensor, w2_svh: torch.Tensor, ptrs: dict | None = None):
         E, two, ht, it, kw = w13_trellis.shape
-        if two != 2 or kw != 48:
-            raise ValueError("w13_trellis must be [E, 2, H/16, I/16, 48] (EXL3 K=3)")
-        if tuple(w2_trellis.shape) != (E, it, ht, 48):
-            raise ValueError("w2_trellis must be [E, I/16, H/16, 48]")
+        if two != 2 or kw not in (32, 48, 64):
+            raise ValueError("w13_trellis must be [E, 2, H/16, I/16, 16*bits] with bits 2, 3 or 4")
+        if tuple(w2_trellis.shape) != (E, it, ht, kw):
+            raise ValueError(f"w2_trellis must be [E, I/16, H/16, {kw}]")
+        self.bits = kw // 16
         H, I = ht * 16, it * 16
         for name, t, shape in (("w13_suh", w13_suh, (E, 2, H)), ("w13_svh", w13_svh, (E, 2, I)),
                                ("w2_suh", w2_suh, (E, I)), ("w2_svh", w2_svh, (E, H))):
@@ -82,13 +83,13 @@ class Exl3MoELayer:
             ptrs = {"gate_trellis": (g0 + ar * s13).to(dev), "up_trellis": (g0 + w13_trellis.stride(1) * 2 + ar * s13).to(dev),
                     "down_trellis": (d0 + ar * w2_trellis.stride(0) * 2).to(dev)}
         self._exl3_ptrs = ptrs
-        self._c = _lib.MoeLayer(E, H, I, 0, ptrs["gate_trellis"].data_ptr(), ptrs["up_trellis"].data_ptr(),
+        self._c = _lib.MoeLayer(E, H, I, self.bits, ptrs["gate_trellis"].data_ptr(), ptrs["up_trellis"].data_ptr(),
                                 ptrs["down_trellis"].data_ptr(), w13_suh.data_ptr(), w13_svh.data_ptr(),
                                 w2_suh.data_ptr(), w2_svh.data_ptr())
 
     @classmethod
     def from_pointer_tables(cls, ptrs: dict, w13_suh: torch.Tensor, w13_svh: torch.Tensor, w2_suh: torch.Tensor,
-                            w2_svh: torch.Tensor) -> "Exl3MoELayer":
+                            w2_svh: torch.Tensor, bits: int = 3) -> "Exl3MoELayer":
         """Layer over expert trellis that live anywhere in device memory: ptrs holds device int64
         [E] address tables 'gate_trellis', 'up_trellis', 'down_trellis' (patch:66-69); the caller keeps
         the trellis storage alive. Addresses must be 16-byte aligned."""
@@ -105,12 +106,15 @@ class Exl3MoELayer:
                 raise ValueError(f"ptrs[{k}] must be int64 [E] on the scales' device")
             if bool(((t % 16) != 0).any()):
                 raise ValueError(f"ptrs[{k}] has an address that is not 16-byte aligned")
+        if bits not in (2, 3, 4):
+            raise ValueError(f"bits {bits} (2, 3 or 4)")
+        self.bits = bits
         self.w13_trellis = self.w2_trellis = None
         self.w13_suh, self.w13_svh, self.w2_suh, self.w2_svh = w13_suh, w13_svh, w2_suh, w2_svh
         self._exl3_num_experts, self._exl3_hidden_size, self._exl3_intermediate_local = E, H, I
         self._exl3_ptrs = {k: ptrs[k].contiguous() for k in ("gate_trellis", "up_trellis", "down_trellis")}
         p = self._exl3_ptrs
-        self._c = _lib.MoeLayer(E, H, I, 0, p["gate_trellis"].data_ptr(), p["up_trellis"].data_ptr(),
+        self._c = _lib.MoeLayer(E, H, I, self.bits, p["gate_trellis"].data_ptr(), p["up_trellis"].data_ptr(),
                                 p["down_trellis"].data_ptr(), w13_suh.data_ptr(), w13_svh.data_ptr(),
                                 w2_suh.data_ptr(), w2_svh.data_ptr())
         return self
@@ -121,16 +125,17 @@ class Exl3MoELayer:
 
     @classmethod
     def synthetic(cls, num_experts: int, hidden: int, intermediate: int, seed: int = 0, layer: int = 0,
-                  device="cuda", expert_range: tuple | None = None) -> "Exl3MoELayer":
-        """Random EXL3 3.0-bpw layer (BASELINE's synthetic weights), generated on the device.
-        expert_range=(lo, hi) builds only experts lo..hi-1 of the num_experts-expert layer (an
-        expert-parallel shard), bit-identical to those experts of the full layer."""
+                  device="cuda", expert_range: tuple | None = None, bits: int = 3) -> "Exl3MoELayer":
+        """Random EXL3 layer (BASELINE's synthetic weights; `bits` per weight, 3 by default),
+        generated on the device. expert_range=(lo, hi) builds only experts lo..hi-1 of the
+        num_experts-expert layer (an expert-parallel shard), bit-identical to those experts of
+        the full layer."""
         E, H, I = num_experts, hidden, intermediate
         lo, hi = expert_range if expert_range is not None else (0, E)
         n = hi - lo
         dev = torch.device(device)
-        w13 = torch.empty((n, 2, H // 16, I // 16, 48), dtype=torch.int16, device=dev)
-        w2 = torch.empty((n, I // 16, H // 16, 48), dtype=torch.int16, device=dev)
+        w13 = torch.empty((n, 2, H // 16, I // 16, 16 * bits), dtype=torch.int16, device=dev)
+        w2 = torch.empty((n, I // 16, H // 16, 16 * bits), dtype=torch.int16, device=dev)
         per13, per2 = w13[0].numel() if n else 0, w2[0].numel() if n else 0
         synth.fill_trellis_torch(w13, seed, synth.STREAM_W13, lo * per13, layer)
         synth.fill_trellis_torch(w2, seed, synth.STREAM_W2, lo * per2, layer)
@@ -140,7 +145,7 @@ class Exl3MoELayer:
     def expert_bytes(self) -> int:
         """Compressed bytes one expert streams per forward (three trellis matrices + fp16 scales)."""
         H, I = self._exl3_hidden_size, self._exl3_intermediate_local
-        return 3 * (H // 16) * (I // 16) * 96 + (2 * H + 2 * I + I + H) * 2
+        return 3 * (H // 16) * (I // 16) * 32 * self.bits + (2 * H + 2 * I + I + H) * 2
 
 
 def as_layer(layer) -> Exl3MoELayer:
@@ -411,14 +416,19 @@ def combine(y: torch.Tensor, route_pos: torch.Tensor, weights: torch.Tensor, out
     return out
 
 
-def decode_dense(trellis: torch.Tensor, k: int, n: int) -> torch.Tensor:
-    """Dense fp16 W [k, n] of one trellis matrix [k/16, n/16, 48] (bit-exact reconstruct)."""
+def decode_dense(trellis: torch.Tensor, k: int, n: int, bits: int | None = None) -> torch.Tensor:
+    """Dense fp16 W [k, n] of one trellis matrix [k/16, n/16, 16*bits] (bit-exact reconstruct);
+    bits (2, 3 or 4) defaults to what the trellis size implies."""
     L = _lib.load()
     t = trellis.contiguous()
-    if t.numel() != (k // 16) * (n // 16) * 48:
-        raise ValueError("trellis size does not match k x n")
+    tiles = (k // 16) * (n // 16)
+    if bits is None:
+        bits = t.numel() // (16 * tiles) if tiles else 3
+    if bits not in (2, 3, 4) or t.numel() != tiles * 16 * bits:
+        raise ValueError("trellis size does not match k x n at 2, 3 or 4 bits per weight")
     w = torch.empty((k, n), dtype=torch.float16, device=t.device)
     with torch.cuda.device(t.device):
-        rc = L.dsv41_decode_dense(t.data_ptr(), k, n, w.data_ptr(), _stream_ptr(torch.cuda.current_stream(t.device)))
-    _lib.check(rc, "dsv41_decode_dense")
+        rc = L.dsv41_decode_dense_bits(t.data_ptr(), k, n, bits, w.data_ptr(),
+                                       _stream_ptr(torch.cuda.current_stream(t.device)))
+    _lib.check(rc, "dsv41_decode_dense_bits")
     return w

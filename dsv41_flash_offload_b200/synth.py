@@ -71,12 +71,13 @@ def trellis_np(seed: int, stream: int, start_word: int, count: int, layer: int =
     return (hash_u32(seed, stream, start_word, count, layer) & np.uint64(0xFFFF)).astype(np.uint16).view(np.int16)
 
 
-def expert_trellis_np(seed: int, H: int, I: int, e: int, layer: int = 0):
-    """(gate, up, down) int16 arrays of expert e in [k/16, n/16, 48] layout."""
-    G = tiles_per_matrix(H, I) * 48
-    gate = trellis_np(seed, STREAM_W13, (2 * e + 0) * G, G, layer).reshape(H // 16, I // 16, 48)
-    up = trellis_np(seed, STREAM_W13, (2 * e + 1) * G, G, layer).reshape(H // 16, I // 16, 48)
-    down = trellis_np(seed, STREAM_W2, e * G, G, layer).reshape(I // 16, H // 16, 48)
+def expert_trellis_np(seed: int, H: int, I: int, e: int, layer: int = 0, bits: int = 3):
+    """(gate, up, down) int16 arrays of expert e in [k/16, n/16, 16*bits] layout."""
+    tw = 16 * bits
+    G = tiles_per_matrix(H, I) * tw
+    gate = trellis_np(seed, STREAM_W13, (2 * e + 0) * G, G, layer).reshape(H // 16, I // 16, tw)
+    up = trellis_np(seed, STREAM_W13, (2 * e + 1) * G, G, layer).reshape(H // 16, I // 16, tw)
+    down = trellis_np(seed, STREAM_W2, e * G, G, layer).reshape(I // 16, H // 16, tw)
     return gate, up, down
 
 

@@ -49,15 +49,15 @@ enum { DSV41_DTYPE_F16 = 0, DSV41_DTYPE_BF16 = 1, DSV41_DTYPE_F32 = 2 };
 
 /* One MoE layer's expert weights, all device pointers (vllm_exl3 Exl3MoEMethod layout,
  * patches/vllm-exl3-host-dma.patch:633-684 and its per-expert pointer tables, patch:66-69):
- *   gate_ptrs/up_ptrs [E]  int64 addresses of int16 trellis [H/16][I/16][48]
- *   down_ptrs [E]          int64 addresses of int16 trellis [I/16][H/16][48]
+ *   gate_ptrs/up_ptrs [E]  int64 addresses of int16 trellis [H/16][I/16][16*bits] (48 at 3 bits)
+ *   down_ptrs [E]          int64 addresses of int16 trellis [I/16][H/16][16*bits]
  *   w13_suh [E][2][H], w13_svh [E][2][I], w2_suh [E][I], w2_svh [E][H]  fp16
  * Every trellis address must be 16-byte aligned. H and I are multiples of 256. */
 typedef struct dsv41_moe_layer {
     int32_t num_experts;
     int32_t hidden;
     int32_t intermediate;
-    int32_t reserved;
+    int32_t bits;       /* bits per weight K of every trellis tile: 2, 3 or 4 (0 = 3, the reference's build) */
     const int64_t* gate_ptrs;
     const int64_t* up_ptrs;
     const int64_t* down_ptrs;
@@ -133,6 +133,9 @@ int dsv41_combine(const void* y, const int32_t* route_pos, const float* weights,
 
 /* Decode one trellis matrix [k/16][n/16][48] int16 into dense fp16 W [k][n] (bit-exact). */
 int dsv41_decode_dense(const void* trellis, int32_t k, int32_t n, void* w_out, void* stream);
+/* Same for K = bits per weight (2, 3 or 4): trellis [k/16][n/16][16*bits] int16 (the 2-bit packs
+ * and 4-bit layers the reference's checkpoints also carry, patch:519-528, pack/prepare_pack.py:47). */
+int dsv41_decode_dense_bits(const void* trellis, int32_t k, int32_t n, int32_t bits, void* w_out, void* stream);
 
 /* Busy-expert GEMM path on pre-permuted rows (run_batch semantics): for each listed expert e
  * with counts[e] rows starting at offsets[e] of token_sorted/weight_sorted, out[token] +=

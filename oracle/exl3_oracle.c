@@ -57,7 +57,14 @@ static inline float r16(float f) { return orc_h2f(orc_f2h(f)); }
  * ------------------------------------------------------------------------------------- */
 #define ORC_MUL1 0x83DCD12Du
 #define ORC_HAD 0.088388347648f
-#define ORC_TILE_WORDS16 48
+
+/* Bits per weight K (3 in the reference's build, ft_core.h:30). The tile format is generic in K
+ * (ft_core.h:63-73 state_scalar is written for any BITS): a 16x16 tile is 16*K int16 words, a
+ * circular 256*K-bit stream. Set once before use (the layer oracle's threads only read it). */
+static int g_bits = 3;
+void orc_set_bits(int bits) { g_bits = (bits == 2 || bits == 4) ? bits : 3; }
+int orc_get_bits(void) { return g_bits; }
+#define ORC_TILE_WORDS16 (16 * g_bits)
 
 int orc_perm(int i)
 {
@@ -73,17 +80,19 @@ int orc_perm(int i)
 
 static inline uint32_t word32(const uint16_t* tile, int w)
 {
-    /* 32-bit little-endian word w (0..23) of the 96-byte tile */
+    /* 32-bit little-endian word w (0..8K-1) of the 32K-byte tile */
     return (uint32_t)tile[2 * w] | ((uint32_t)tile[2 * w + 1] << 16);
 }
 
 uint16_t orc_state(const uint16_t* tile, int t)
 {
-    /* The tile is a circular 768-bit stream read MSB-first through its 24 words; the state of
-     * symbol t is the 16-bit window ending at stream bit 3t+2, i.e. starting at 3t-13. */
-    const int start = (3 * t - 13 + 768) % 768;
+    /* The tile is a circular 256K-bit stream read MSB-first through its 8K words; the state of
+     * symbol t is the 16-bit window ending at stream bit K*t+K-1, i.e. starting at K*t+K-16
+     * (K = 3: 768 bits, 24 words, start 3t-13). */
+    const int K = g_bits, nbits = 256 * K, nwords = 8 * K;
+    const int start = (K * t + K - 16 + nbits) % nbits;
     const int a = start >> 5, o = start & 31;
-    const uint64_t win = ((uint64_t)word32(tile, a) << 32) | word32(tile, (a + 1) % 24);
+    const uint64_t win = ((uint64_t)word32(tile, a) << 32) | word32(tile, (a + 1) % nwords);
     return (uint16_t)((win >> (48 - o)) & 0xffffu);
 }
 
@@ -103,7 +112,7 @@ uint16_t orc_weight_bits(uint16_t state)
 
 void orc_decode_matrix(const uint16_t* trellis, int k, int n, uint16_t* W)
 {
-    /* dense_weights (ft_core.h:977-992): tile (tk, tn) at [k/16][n/16][48] */
+    /* dense_weights (ft_core.h:977-992): tile (tk, tn) at [k/16][n/16][16K] */
     const int tn_count = n / 16;
     for (int tk = 0; tk < k / 16; ++tk)
         for (int tn = 0; tn < tn_count; ++tn) {

@@ -32,9 +32,12 @@ int orc_perm(int i);
 uint16_t orc_state(const uint16_t* tile, int t);
 /* byte sum of state * 0x83DCD12D (0..1020) */
 int orc_bytesum(uint16_t state);
+/* bits per weight K of the trellis tiles (2, 3 or 4; default 3 = the reference's build) */
+void orc_set_bits(int bits);
+int orc_get_bits(void);
 /* fp16 bits of the decoded weight for one state */
 uint16_t orc_weight_bits(uint16_t state);
-/* whole matrix: trellis [k/16][n/16][48] int16 -> W [k][n] fp16 bits */
+/* whole matrix: trellis [k/16][n/16][16K] int16 -> W [k][n] fp16 bits */
 void orc_decode_matrix(const uint16_t* trellis, int k, int n, uint16_t* W);
 
 /* transforms on one 128-block (fp32 math, fp16 rounding points) */

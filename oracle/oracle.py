@@ -48,6 +48,8 @@ class Oracle:
         L = C.CDLL(path)
         L.orc_h2f.restype = C.c_float
         L.orc_h2f.argtypes = [C.c_uint16]
+        L.orc_set_bits.argtypes = [C.c_int]
+        L.orc_get_bits.restype = C.c_int
         L.orc_f2h.restype = C.c_uint16
         L.orc_f2h.argtypes = [C.c_float]
         L.orc_perm.restype = C.c_int
@@ -73,6 +75,14 @@ class Oracle:
         L.orc_moe_routes.argtypes = common + [C.c_int, C.c_int, C.c_void_p, C.c_int] + \
             [C.c_void_p] * 7 + [C.c_float, C.c_int, C.c_void_p]
         self.L = L
+
+    def set_bits(self, bits: int) -> None:
+        """Bits per weight K of the trellis tiles (2, 3 or 4) for every following call."""
+        self.L.orc_set_bits(int(bits))
+
+    @property
+    def bits(self) -> int:
+        return self.L.orc_get_bits()
 
     # --- format -------------------------------------------------------------------------
     def weight_table(self) -> np.ndarray:

@@ -27,5 +27,10 @@ def oracle_out(oracle, layer, x, ids, w, limit=0.0, expert_map=None, per_route=F
     s13, v13, s2, v2 = layer_numpy_scales(layer)
     xf = x.detach().to(torch.float16).float().cpu().numpy()
     wn = None if w is None else w.detach().float().cpu().numpy()
-    return oracle.moe_layer(xf, ids_np, wn, gate, up, down, s13, v13, s2, v2, limit=limit, expert_map=emap,
-                            per_route=per_route)
+    prev = oracle.bits
+    oracle.set_bits(getattr(layer, "bits", 3))
+    try:
+        return oracle.moe_layer(xf, ids_np, wn, gate, up, down, s13, v13, s2, v2, limit=limit, expert_map=emap,
+                                per_route=per_route)
+    finally:
+        oracle.set_bits(prev)
