@@ -9,8 +9,8 @@ gives bits, codebook and per-layer `layer_bits` overrides.
 
 `load_moe_layer` stacks one layer's experts (or an expert-parallel shard of them) into vllm_exl3's
 layout (w13_trellis [E, 2, H/16, I/16, 48], w2_trellis [E, I/16, H/16, 48], w13_suh [E, 2, H], ...,
-patch:633-684) on the device, ready for apply_exl3_fused_moe. Only the mul1 codebook at 3 bits is
-accepted (what the kernels decode); other layers raise NotImplementedError. The safetensors format
+patch:633-684) on the device, ready for apply_exl3_fused_moe. The mul1 codebook at 2, 3 or 4 bits
+per weight is accepted (what the kernels decode); other layers raise NotImplementedError. The safetensors format
 is parsed here directly (8-byte little-endian header length, JSON header, raw little-endian data),
 so nothing beyond numpy and torch is needed; `write_safetensors` is the matching writer.
 """
@@ -145,8 +145,8 @@ def load_moe_layer(path_or_ckpt, layer: int, device="cuda", expert_range: tuple 
     if q.get("codebook", "mul1") != "mul1":
         raise NotImplementedError(f"codebook {q.get('codebook')!r}: the kernels decode the mul1 codebook")
     bits = ck.layer_bits(layer)
-    if bits != 3:
-        raise NotImplementedError(f"layer {layer} is {bits}-bit; the kernels decode 3-bit (K=3) trellis")
+    if bits not in (2, 3, 4):
+        raise NotImplementedError(f"layer {layer} is {bits}-bit; the kernels decode 2, 3 or 4 bits per weight")
     prefix, ids = ck.expert_ids(layer)
     E = ids[-1] + 1
     if ids != list(range(E)):
@@ -157,13 +157,14 @@ def load_moe_layer(path_or_ckpt, layer: int, device="cuda", expert_range: tuple 
     base = lambda e, w: f"{prefix}layers.{layer}.ffn.experts.{e}.{w}"
     t1 = ck.tensor(base(0, "w1") + ".trellis")
     Ht, It, kw = t1.shape
-    if kw != 48 or t1.dtype != np.int16:
-        raise ValueError(f"w1 trellis of layer {layer} is {t1.dtype} {t1.shape}; expected int16 [H/16, I/16, 48]")
+    if kw != 16 * bits or t1.dtype != np.int16:
+        raise ValueError(f"w1 trellis of layer {layer} is {t1.dtype} {t1.shape}; expected int16 "
+                         f"[H/16, I/16, {16 * bits}] at {bits} bits")
     H, I = Ht * 16, It * 16
     n = hi - lo
     dev = torch.device(device)
-    w13 = torch.empty((n, 2, Ht, It, 48), dtype=torch.int16, device=dev)
-    w2 = torch.empty((n, It, Ht, 48), dtype=torch.int16, device=dev)
+    w13 = torch.empty((n, 2, Ht, It, kw), dtype=torch.int16, device=dev)
+    w2 = torch.empty((n, It, Ht, kw), dtype=torch.int16, device=dev)
     suh13 = torch.empty((n, 2, H), dtype=torch.float16, device=dev)
     svh13 = torch.empty((n, 2, I), dtype=torch.float16, device=dev)
     suh2 = torch.empty((n, I), dtype=torch.float16, device=dev)
@@ -179,12 +180,12 @@ def load_moe_layer(path_or_ckpt, layer: int, device="cuda", expert_range: tuple 
         for w, m in (("w1", 0), ("w3", 1)):
             key = base(e, w)
             _check_codebook(ck, key)
-            put(w13[j, m], key + ".trellis", (Ht, It, 48), np.int16)
+            put(w13[j, m], key + ".trellis", (Ht, It, kw), np.int16)
             put(suh13[j, m], key + ".suh", (H,), np.float16)
             put(svh13[j, m], key + ".svh", (I,), np.float16)
         key = base(e, "w2")
         _check_codebook(ck, key)
-        put(w2[j], key + ".trellis", (It, Ht, 48), np.int16)
+        put(w2[j], key + ".trellis", (It, Ht, kw), np.int16)
         put(suh2[j], key + ".suh", (I,), np.float16)
         put(svh2[j], key + ".svh", (H,), np.float16)
     return Exl3MoELayer(w13, w2, suh13, svh13, suh2, svh2)

@@ -14,12 +14,12 @@ from dsv41_flash_offload_b200 import loader, synth
 E, H, I, LAYER = 3, 256, 256, 5
 
 
-def _write_ckpt(d, prefix="model.", bits_override=None, mcg=False, bad_mul1=False):
+def _write_ckpt(d, prefix="model.", bits_override=None, mcg=False, bad_mul1=False, bits=3):
     s13, v13, s2, v2 = synth.scales_np(9, E, H, I, LAYER)
     shards = [{}, {}]
     wm = {}
     for e in range(E):
-        g, u, dn = synth.expert_trellis_np(9, H, I, e, LAYER)
+        g, u, dn = synth.expert_trellis_np(9, H, I, e, LAYER, bits=bits)
         for w, tr, suh, svh in (("w1", g, s13[e, 0], v13[e, 0]), ("w3", u, s13[e, 1], v13[e, 1]), ("w2", dn, s2[e], v2[e])):
             key = f"{prefix}layers.{LAYER}.ffn.experts.{e}.{w}"
             sh = shards[e % 2]
@@ -34,7 +34,7 @@ def _write_ckpt(d, prefix="model.", bits_override=None, mcg=False, bad_mul1=Fals
         loader.write_safetensors(os.path.join(d, fn), sh)
         wm.update({k: fn for k in sh})
     json.dump({"metadata": {}, "weight_map": wm}, open(os.path.join(d, "model.safetensors.index.json"), "w"))
-    q = {"quant_method": "exl3", "bits": 3, "codebook": "mul1", "layer_bits": {str(LAYER + 1): 4}}
+    q = {"quant_method": "exl3", "bits": bits, "codebook": "mul1", "layer_bits": {str(LAYER + 1): 4}}
     if bits_override:
         q["layer_bits"][str(LAYER)] = bits_override
     json.dump({"quantization_config": q}, open(os.path.join(d, "config.json"), "w"))
@@ -57,11 +57,11 @@ def test_loader_round_trip_cpu(tmp_path):
 
 
 def test_loader_rejects_unsupported(tmp_path):
-    for i, kw in enumerate(({"bits_override": 2}, {"mcg": True}, {"bad_mul1": True})):
+    for i, kw in enumerate(({"bits_override": 5}, {"mcg": True}, {"bad_mul1": True}, {"bits_override": 2})):
         d = tmp_path / str(i)
         d.mkdir()
         _write_ckpt(str(d), **kw)
-        with pytest.raises(NotImplementedError):
+        with pytest.raises(ValueError if i == 3 else NotImplementedError):   # 2-bit config, 3-bit tiles
             loader.load_moe_layer(str(d), LAYER, device="cpu")
     ok = tmp_path / "ok"
     ok.mkdir()
@@ -93,3 +93,10 @@ def test_loaded_layer_matches_synthetic_on_gpu(tmp_path):
     ids, w = torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda()
     assert torch.equal(exl3.apply_exl3_fused_moe(x, ids, w, lay, None, None, 10.0),
                        exl3.apply_exl3_fused_moe(x, ids, w, ref, None, None, 10.0))
+
+
+def test_loader_four_bit_layer(tmp_path):
+    _write_ckpt(str(tmp_path), bits=4)
+    lay = loader.load_moe_layer(str(tmp_path), LAYER, device="cpu")
+    g, u, dn = synth.expert_trellis_np(9, H, I, 2, LAYER, bits=4)
+    assert lay.bits == 4 and np.array_equal(lay.w13_trellis[2, 1].numpy(), u) and np.array_equal(lay.w2_trellis[2].numpy(), dn)
