@@ -188,6 +188,21 @@ __device__ __forceinline__ void had128_warp(float (&v)[4], int lane)
     }
 }
 
+// 128-point Hadamard of one row held by one thread, stage order w = 1..64 (ft_core.h:89-94)
+__device__ __forceinline__ void had128_thread(float (&v)[128])
+{
+#pragma unroll
+    for (int w = 1; w < 128; w <<= 1)
+#pragma unroll
+        for (int b = 0; b < 128; b += 2 * w)
+#pragma unroll
+            for (int i = b; i < b + w; ++i) {
+                const float p = v[i], q = v[i + w];
+                v[i] = p + q;
+                v[i + w] = p - q;
+            }
+}
+
 // silu(g) with the reference's clamp (u to [-L, L], silu from above; L = 0 disables),
 // ft_core.h:123-133
 __device__ __forceinline__ float act_gu(float g, float u, float limit)

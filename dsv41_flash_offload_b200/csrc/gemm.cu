@@ -180,21 +180,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
         : "memory");
 }
 
-// 128-point Hadamard of one row held by one thread, stage order w = 1..64 (ft_core.h:89-94)
-__device__ __forceinline__ void had128_thread(float (&v)[128])
-{
-#pragma unroll
-    for (int w = 1; w < 128; w <<= 1)
-#pragma unroll
-        for (int b = 0; b < 128; b += 2 * w)
-#pragma unroll
-            for (int i = b; i < b + w; ++i) {
-                const float p = v[i], q = v[i + w];
-                v[i] = p + q;
-                v[i + w] = p - q;
-            }
-}
-
 __device__ __forceinline__ void load_half8(const __half* p, float* dst)
 {
     const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
