@@ -44,6 +44,13 @@ constexpr int kGemmThreads = (kWarpDec0 + kDecWarps) * 32;   // 384
 #define DSV41_GEMM_DEC_UNROLL 4
 #endif
 constexpr int kDecUnroll = DSV41_GEMM_DEC_UNROLL;   // tiles of the decode loop in flight per warp
+#ifndef DSV41_GEMM_MERGED_RING
+#define DSV41_GEMM_MERGED_RING 1
+#endif
+// 1: the activation and decoded-weight stages advance together under one full barrier (TMA bytes +
+// one arrival per decoder warp) and one empty barrier, so the MMA thread waits once and commits once
+// per chunk (each wait and commit of the issuing thread costs the tensor pipe a few hundred cycles)
+constexpr bool kMergedRing = DSV41_GEMM_MERGED_RING != 0;
 constexpr int kBM = 128;        // rows per M tile (TMEM lanes)
 constexpr int kBN = 128;        // features per unit (TMEM columns per accumulator)
 #ifndef DSV41_GEMM_BK
@@ -77,7 +84,7 @@ struct GemmCfg {
     static constexpr int b_bytes = nmat * kTileB;
     static constexpr int t_bytes = nmat * kKT * tr_row<K>();
     static constexpr int a_stages = 2 * (64 / kBK);
-    static constexpr int b_stages = (MODE == 0 ? 2 : 3) * (64 / kBK);
+    static constexpr int b_stages = kMergedRing ? a_stages : (MODE == 0 ? 2 : 3) * (64 / kBK);
     static constexpr int t_stages = (MODE == 0 ? 4 : 8) * (64 / kBK);
     static constexpr int a_off = 0;
     static constexpr int b_off = a_off + a_stages * a_bytes;
@@ -238,7 +245,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < AS; ++s) {
-            mbar_init(&a_full[s], 1);
+            mbar_init(&a_full[s], kMergedRing ? 1 + kDecWarps : 1);
             mbar_init(&a_empty[s], 1);
         }
         for (int s = 0; s < BS; ++s) {
@@ -362,7 +369,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 const int act_mt = (p.passes[u / n_fb].z + kBM - 1) / kBM;
                 for (int c = 0; c < n_chunks; ++c, ++ia, ++ib) {
                     const int sa = ia % AS, sb = ib % BS;
-                    if (!mbar_wait_bounded(&b_full[sb], (ib / BS) & 1, abort_flag, p.status) ||
+                    if ((!kMergedRing && !mbar_wait_bounded(&b_full[sb], (ib / BS) & 1, abort_flag, p.status)) ||
                         !mbar_wait_bounded(&a_full[sa], (ia / AS) & 1, abort_flag, p.status)) {
                         ok = false;
                         break;
@@ -385,7 +392,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                         }
                     }
                     umma_commit(&a_empty[sa]);
-                    umma_commit(&b_empty[sb]);
+                    if (!kMergedRing) umma_commit(&b_empty[sb]);
                 }
                 if (ok) umma_commit(acc_full);
             }
@@ -393,7 +400,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
             if (ib > 0) {
                 const uint32_t j = ib - 1;
                 const uint64_t t0 = globaltimer_ns();
-                while (!mbar_try_wait(&b_empty[j % BS], (j / BS) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {}
+                uint64_t* last = kMergedRing ? &a_empty[j % AS] : &b_empty[j % BS];
+                while (!mbar_try_wait(last, (j / BS) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {}
             }
         }
         __syncwarp();
@@ -431,7 +439,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
             for (int c = 0; c < n_chunks; ++c, ++it, ++ib) {
                 const int st = it % TS, sb = ib % BS;
                 if (!mbar_wait_bounded(&t_full[st], (it / TS) & 1, abort_flag, p.status) ||
-                    !mbar_wait_bounded(&b_empty[sb], ((ib / BS) & 1) ^ 1, abort_flag, p.status)) {
+                    !mbar_wait_bounded(kMergedRing ? &a_empty[sb] : &b_empty[sb], ((ib / BS) & 1) ^ 1, abort_flag,
+                                       p.status)) {
                     ok = false;
                     break;
                 }
@@ -448,7 +457,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(&b_full[sb]);
+                    mbar_arrive(kMergedRing ? &a_full[sb] : &b_full[sb]);
                     mbar_arrive(&t_empty[st]);
                 }
             }
