@@ -11,7 +11,7 @@
 // trellis words):
 //   warp 0     activation producer: TMA (cp.async.bulk.tensor, SWIZZLE_128B, into this CTA only) of
 //              128-row x 64-k tiles; a stage is reused once the MMAs that read it have committed
-//   warp 1     TMEM allocator (512 columns) and single-thread tcgen05.mma issuer
+//   warps 1, 3 TMEM allocator (warp 1, 512 columns) and two single-thread tcgen05.mma issuers
 //              (kind::f16, M=128, N=128, K=16, fp32 accumulators in TMEM); tcgen05.commit releases
 //              the activation and weight stages and signals the finished accumulators
 //   warp 2     trellis producer: 1-D bulk copies of the compressed k-rows into a 4-8 stage ring
@@ -31,13 +31,14 @@
 namespace dsv41 {
 
 // warp roles
-// (warp w issues on SM sub-partition w % 4 and may only touch TMEM lanes 32*(w%4)..+31: the three
-// producer/issuer warps and the idle warp 3 take one sub-partition each, so every sub-partition
-// runs one of them plus two decoders, and the decoders cover each TMEM lane quarter twice)
+// (warp w issues on SM sub-partition w % 4 and may only touch TMEM lanes 32*(w%4)..+31: the two
+// producers and two MMA issuers take one sub-partition each, so every sub-partition runs one of
+// them plus two decoders, and the decoders cover each TMEM lane quarter twice)
 constexpr int kWarpA = 0;        // TMA producer of the activation tiles
 constexpr int kWarpMma = 1;      // TMEM allocator + single-thread tcgen05.mma issuer
 constexpr int kWarpT = 2;        // bulk-copy producer of the trellis k-rows
-constexpr int kWarpDec0 = 4;     // warps 4..11: decoders, then epilogue (warp 3 idles)
+constexpr int kWarpMma2 = 3;     // second MMA issuer (merged ring)
+constexpr int kWarpDec0 = 4;     // warps 4..11: decoders, then epilogue
 constexpr int kDecWarps = 8;
 constexpr int kGemmThreads = (kWarpDec0 + kDecWarps) * 32;   // 384
 #ifndef DSV41_GEMM_DEC_UNROLL
@@ -51,6 +52,11 @@ constexpr int kDecUnroll = DSV41_GEMM_DEC_UNROLL;   // tiles of the decode loop 
 // one arrival per decoder warp) and one empty barrier, so the MMA thread waits once and commits once
 // per chunk (each wait and commit of the issuing thread costs the tensor pipe a few hundred cycles)
 constexpr bool kMergedRing = DSV41_GEMM_MERGED_RING != 0;
+// Two threads issue the MMAs, each for its own accumulators ((M tile, matrix) pairs alternate): every
+// wait -> MMAs -> commit cycle of one issuing thread leaves the tensor pipe idle for ~500 cycles
+// (measured on B200, independent of the group size), and the other thread's MMAs fill that gap
+// (probe: 16-MMA groups at 97 cycles per MMA with one issuer, 64 with two; ideal 64).
+constexpr int kIssuers = kMergedRing ? 2 : 1;
 constexpr int kBM = 128;        // rows per M tile (TMEM lanes)
 constexpr int kBN = 128;        // features per unit (TMEM columns per accumulator)
 #ifndef DSV41_GEMM_BK
@@ -242,11 +248,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
     const int n_chunks = p.K / kBK;
     const int n_units = (*p.n_passes) * n_fb;
     const int ntile_row = p.N / 16;
+    // no busy expert in this call (the usual decode case): leave before allocating TMEM
+    if (n_units <= (int)blockIdx.x) return;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < AS; ++s) {
             mbar_init(&a_full[s], kMergedRing ? 1 + kDecWarps : 1);
-            mbar_init(&a_empty[s], 1);
+            mbar_init(&a_empty[s], kIssuers);
         }
         for (int s = 0; s < BS; ++s) {
             mbar_init(&b_full[s], kDecWarps);
@@ -256,7 +264,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
             mbar_init(&t_full[s], 1);
             mbar_init(&t_empty[s], kDecWarps);
         }
-        mbar_init(acc_full, 1);
+        mbar_init(acc_full, kIssuers);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -354,13 +362,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
             }
         }
         __syncwarp();
-    } else if (warp == kWarpMma) {
-        // ---------------------------------- MMA issuer ----------------------------------
+    } else if (warp == kWarpMma || (kIssuers == 2 && warp == kWarpMma2)) {
+        // ---------------------------------- MMA issuers ----------------------------------
+        const int me = warp == kWarpMma ? 0 : 1;
         if (lane == 0) {
             uint32_t ia = 0, ib = 0;
             bool ok = true;
-            // One thread issues every MMA, so its per-MMA instruction count bounds the tensor
-            // pipe: the descriptors of stage 0 are built once, and a stage / tile / k step only
+            // A single thread issues each accumulator's MMAs, so its per-MMA instruction count
+            // matters: the descriptors of stage 0 are built once, and a stage / tile / k step only
             // adds its byte offset / 16 to the 14-bit start-address field (shared memory stays
             // below 256 KB, so the field never carries).
             const uint64_t adesc0 = sw_desc(smem_addr(smem + Cfg::a_off));
@@ -378,11 +387,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                     const uint64_t ad_s = adesc0 + (uint64_t)((sa * Cfg::a_bytes) >> 4);
                     const uint64_t bd_s = bdesc0 + (uint64_t)((sb * Cfg::b_bytes) >> 4);
                     const uint32_t acc0 = c > 0 ? 1u : 0u;
+                    int issued = 0;
 #pragma unroll
                     for (int mt = 0; mt < Cfg::mtiles; ++mt) {
                         if (mt >= act_mt) break;
 #pragma unroll
                         for (int mat = 0; mat < Cfg::nmat; ++mat) {
+                            if ((mt * Cfg::nmat + mat) % kIssuers != me) continue;
+                            ++issued;
                             const uint32_t d = tmem + (uint32_t)((mt * Cfg::nmat + mat) * kBN);
                             const uint64_t ad = ad_s + (uint64_t)(((mat * Cfg::mtiles + mt) * kTileA) >> 4);
                             const uint64_t bd = bd_s + (uint64_t)((mat * kTileB) >> 4);
@@ -391,7 +403,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                                 umma_f16(d, ad + 2 * kk, bd + 2 * kk, kk ? 1u : acc0);
                         }
                     }
-                    umma_commit(&a_empty[sa]);
+                    if (issued)
+                        umma_commit(&a_empty[sa]);
+                    else
+                        mbar_arrive(&a_empty[sa]);   // nothing of this stage read by this issuer
                     if (!kMergedRing) umma_commit(&b_empty[sb]);
                 }
                 if (ok) umma_commit(acc_full);

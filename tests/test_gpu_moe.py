@@ -268,3 +268,20 @@ def test_vllm_plugin_and_decode_graphs(layer_small):
         out = dg(x, ids, w)
         assert torch.equal(out, exl3.apply_exl3_fused_moe(x, ids, w, layer_small, None, None, LIMIT)), t
     dg.close()
+
+
+def test_gemm_many_rows_per_expert_vs_oracle(oracle):
+    """Busy experts with many row passes (over 768 rows each), and more than 48 of them, vs oracle."""
+    lay = exl3.Exl3MoELayer.synthetic(16, 512, 256, seed=8, device=DEV)
+    x, ids, w = _inputs(71, 1000, 512, 16, 4, kind="zipf", zipf_s=2.0)
+    counts = torch.bincount(ids.reshape(-1), minlength=16)
+    assert int(counts.max()) > 768
+    out = exl3.apply_exl3_fused_moe(x, ids, w, lay, None, None, LIMIT, fat_threshold=32)
+    assert exl3.read_status(device=DEV) == 0
+    assert_close_layer(out.cpu().numpy(), oracle_out(oracle, lay, x, ids, w, LIMIT), "many passes")
+    lay2 = exl3.Exl3MoELayer.synthetic(64, 256, 256, seed=9, device=DEV)
+    x, ids, w = _inputs(72, 8000, 256, 64, 8)
+    assert int((torch.bincount(ids.reshape(-1), minlength=64) > 768).sum()) > 48
+    out = exl3.apply_exl3_fused_moe(x, ids, w, lay2, None, None, LIMIT, fat_threshold=32)
+    assert exl3.read_status(device=DEV) == 0
+    assert_close_layer(out.cpu().numpy(), oracle_out(oracle, lay2, x, ids, w, LIMIT), "many busy experts")
