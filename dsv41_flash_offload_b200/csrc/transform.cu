@@ -11,24 +11,95 @@
 
 namespace dsv41 {
 
-// one warp task = (sorted row p, 128-block b): both gate and up transforms of that block
-// rows p < *nrows; rows whose expert_sorted entry is negative are skipped
-__global__ void __launch_bounds__(256) prep_kernel(const XRows x, int x_dtype, const int* token_sorted,
+// 8 consecutive columns of row `idx` (any of the three ABI dtypes) rounded to fp16, as floats
+__device__ __forceinline__ void load8_as_half(const void* x, int dtype, size_t idx, float (&v)[8])
+{
+    if (dtype == 2) {
+        const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + idx);
+        const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + idx + 4);
+        v[0] = r16(a.x); v[1] = r16(a.y); v[2] = r16(a.z); v[3] = r16(a.w);
+        v[4] = r16(b.x); v[5] = r16(b.y); v[6] = r16(b.z); v[7] = r16(b.w);
+        return;
+    }
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + idx);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (dtype == 0) {
+            const __half2 h = u32_as_half2(w[q]);
+            v[2 * q] = __low2float(h);
+            v[2 * q + 1] = __high2float(h);
+        } else {
+            v[2 * q] = r16(__uint_as_float(w[q] << 16));
+            v[2 * q + 1] = r16(__uint_as_float(w[q] & 0xffff0000u));
+        }
+    }
+}
+
+__device__ __forceinline__ void load8_half(const __half* p, float (&v)[8])
+{
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const __half2 h = u32_as_half2(w[q]);
+        v[2 * q] = __low2float(h);
+        v[2 * q + 1] = __high2float(h);
+    }
+}
+
+__device__ __forceinline__ void store8_half(__half* p, const float (&v)[8])
+{
+    uint4 u;
+    u.x = half2_as_u32(__floats2half2_rn(v[0], v[1]));
+    u.y = half2_as_u32(__floats2half2_rn(v[2], v[3]));
+    u.z = half2_as_u32(__floats2half2_rn(v[4], v[5]));
+    u.w = half2_as_u32(__floats2half2_rn(v[6], v[7]));
+    *reinterpret_cast<uint4*>(p) = u;
+}
+
+// 128-point Hadamard of one block held by 16 lanes x 8 consecutive values (element 8*hl + q): stages
+// w = 1, 2, 4 inside the thread, then w = 8 .. 64 across lanes hl ^ 1 .. hl ^ 8, the same pairs and
+// order as the reference's had128 (ft_core.h:89-94); the two half-warps transform independent blocks
+__device__ __forceinline__ void had128_half(float (&v)[8], int hl)
+{
+#pragma unroll
+    for (int w = 1; w < 8; w <<= 1)
+#pragma unroll
+        for (int b = 0; b < 8; b += 2 * w)
+#pragma unroll
+            for (int i = b; i < b + w; ++i) {
+                const float a = v[i], c = v[i + w];
+                v[i] = a + c;
+                v[i + w] = a - c;
+            }
+#pragma unroll
+    for (int m = 1; m < 16; m <<= 1) {
+        const bool upper = (hl & m) != 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float pv = __shfl_xor_sync(0xffffffffu, v[q], m);
+            v[q] = upper ? (pv - v[q]) : (v[q] + pv);
+        }
+    }
+}
+
+// one warp per sorted row p (rows p < *nrows; rows whose expert_sorted entry is negative are skipped):
+// half-warp h transforms 128-blocks 2j + h of the row for gate and up,
+//   xt_{g,u}[p] = fp16(H128(fp16(x[token]) * suh_{g,u}) * 2^-3.5)
+// with 16-byte loads and stores; the row's indices are read once
+__global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ XRows x, int x_dtype, const int* token_sorted,
                                                    const int* expert_sorted, const int* nrows,
                                                    const __half* w13_suh, int H, __half* xt_g, __half* xt_u)
 {
-    const int lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
     const int nvalid = *nrows;
-    const int nb = H / 128;
-    const long long tasks = (long long)nvalid * nb;
-    const long long wstride = (long long)gridDim.x * (blockDim.x >> 5);
-    for (long long tk = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tk < tasks; tk += wstride) {
-        const int p = (int)(tk / nb), b = (int)(tk % nb);
+    const int nb = H / 128, npair = (nb + 1) / 2;
+    const int wstride = gridDim.x * (blockDim.x >> 5);
+    for (int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < nvalid; p += wstride) {
         const int e = expert_sorted[p];
         if (e < 0) continue;
         const int t = token_sorted[p];
-        const int c = b * 128 + lane * 4;
-        float xv[4];
         // token t's row: the caller's rows, or (expert parallel) row t % per of rank t / per
         const void* xb = x.base[0];
         size_t row = (size_t)t;
@@ -36,17 +107,27 @@ __global__ void __launch_bounds__(256) prep_kernel(const XRows x, int x_dtype, c
             xb = x.base[t / x.per];
             row = (size_t)(t % x.per);
         }
-        load4_as_half(xb, x_dtype, row * H + c, xv);
+        const __half* sg = w13_suh + (size_t)e * 2 * H;
+        __half* og = xt_g + (size_t)p * H;
+        __half* ou = xt_u + (size_t)p * H;
+#pragma unroll 2
+        for (int j = 0; j < npair; ++j) {
+            const int blk = 2 * j + half;
+            const bool act = blk < nb;   // an odd last block leaves the upper half-warp computing a copy
+            const int c = (act ? blk : blk - 1) * 128 + hl * 8;
+            float xv[8];
+            load8_as_half(xb, x_dtype, row * H + c, xv);
 #pragma unroll
-        for (int m = 0; m < 2; ++m) {
-            float s[4], v[4];
-            load4_half(w13_suh + ((size_t)e * 2 + m) * H + c, s);
+            for (int m = 0; m < 2; ++m) {
+                float s[8], v[8];
+                load8_half(sg + (size_t)m * H + c, s);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(xv[q], s[q]);
-            had128_warp(v, lane);
+                for (int q = 0; q < 8; ++q) v[q] = __fmul_rn(xv[q], s[q]);
+                had128_half(v, hl);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(v[q], kHad);
-            store4_half((m ? xt_u : xt_g) + (size_t)p * H + c, v);
+                for (int q = 0; q < 8; ++q) v[q] = __fmul_rn(v[q], kHad);
+                if (act) store8_half((m ? ou : og) + c, v);
+            }
         }
     }
 }
@@ -66,8 +147,7 @@ cudaError_t launch_prep_rows(const XRows& x, int x_dtype, const int* token_sorte
                              const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
                              cudaStream_t st)
 {
-    const long long tasks = (long long)N * (H / 128);
-    long long blocks = (tasks + 7) / 8;
+    long long blocks = ((long long)N + 7) / 8;   // one warp per sorted row
     const long long cap = (long long)num_sms() * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
