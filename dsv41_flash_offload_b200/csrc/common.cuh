@@ -166,6 +166,13 @@ __device__ __forceinline__ void decode_tile(const uint32_t* tw, const LaneDec<K>
 // had128, ft_core.h:89-94, so every fp32 intermediate is the same)
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ float r16(float f) { return __half2float(__float2half_rn(f)); }
+// the same rounding of two values through one packed f32x2 -> f16x2 conversion
+__device__ __forceinline__ void r16x2(float& a, float& b)
+{
+    const float2 f = __half22float2(__floats2half2_rn(a, b));
+    a = f.x;
+    b = f.y;
+}
 
 __device__ __forceinline__ void had128_warp(float (&v)[4], int lane)
 {
@@ -203,11 +210,22 @@ __device__ __forceinline__ void had128_thread(float (&v)[128])
             }
 }
 
+// 1: silu's exp and division use the hardware exp2 / reciprocal approximations (a few fp32 ulp from
+// the libm expf and IEEE division of the reference's CPU tier, before the result is rounded to fp16;
+// the layer tolerance is 2e-2 max-abs / cosine 0.9999). Measured on B200: the busy-expert epilogue's
+// SwiGLU step drops from ~18k to ~7.4k cycles per 128-feature block. 0: the exact library forms.
+#ifndef DSV41_FAST_ACT
+#define DSV41_FAST_ACT 1
+#endif
 // silu(g) with the reference's clamp (u to [-L, L], silu from above; L = 0 disables),
 // ft_core.h:123-133
 __device__ __forceinline__ float act_gu(float g, float u, float limit)
 {
+#if DSV41_FAST_ACT
+    float s = __fdividef(g, 1.0f + __expf(-g));
+#else
     float s = g / (1.0f + expf(-g));
+#endif
     if (limit != 0.0f) {
         u = fminf(fmaxf(u, -limit), limit);
         s = fminf(s, limit);

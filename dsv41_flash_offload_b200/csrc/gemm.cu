@@ -214,14 +214,16 @@ __device__ __forceinline__ void load_half8(const __half* p, float* dst)
 __device__ __forceinline__ void out_block128(float (&v)[128], const __half* svh)
 {
 #pragma unroll
-    for (int i = 0; i < 128; ++i) v[i] = r16(v[i]);
+    for (int i = 0; i < 128; i += 2) r16x2(v[i], v[i + 1]);
     had128_thread(v);
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
         float s[8];
         load_half8(svh + c * 8, s);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) v[c * 8 + q] = r16(__fmul_rn(__fmul_rn(v[c * 8 + q], kHad), s[q]));
+        for (int q = 0; q < 8; ++q) v[c * 8 + q] = __fmul_rn(__fmul_rn(v[c * 8 + q], kHad), s[q]);
+#pragma unroll
+        for (int q = 0; q < 8; q += 2) r16x2(v[c * 8 + q], v[c * 8 + q + 1]);
     }
 }
 
@@ -262,8 +264,13 @@ __device__ __forceinline__ void gateup_epilogue(float (&v)[128], uint32_t tg, ui
             float s8[8];
             load_half8(sd + q * 32 + c8 * 8, s8);
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                g[c8 * 8 + i] = __fmul_rn(r16(act_gu(g[c8 * 8 + i], uu[c8 * 8 + i], limit)), s8[i]);
+            for (int i = 0; i < 8; i += 2) {
+                float a0 = act_gu(g[c8 * 8 + i], uu[c8 * 8 + i], limit);
+                float a1 = act_gu(g[c8 * 8 + i + 1], uu[c8 * 8 + i + 1], limit);
+                r16x2(a0, a1);
+                g[c8 * 8 + i] = __fmul_rn(a0, s8[i]);
+                g[c8 * 8 + i + 1] = __fmul_rn(a1, s8[i + 1]);
+            }
         }
         tmem_st32(tg + q * 32, g);
     }

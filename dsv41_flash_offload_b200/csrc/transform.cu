@@ -58,15 +58,15 @@ __device__ __forceinline__ void store8_half(__half* p, const float (&v)[8])
     *reinterpret_cast<uint4*>(p) = u;
 }
 
-// 128-point Hadamard of one block held by 16 lanes x 8 consecutive values (element 8*hl + q): stages
-// w = 1, 2, 4 inside the thread, then w = 8 .. 64 across lanes hl ^ 1 .. hl ^ 8, the same pairs and
-// order as the reference's had128 (ft_core.h:89-94); the two half-warps transform independent blocks
-__device__ __forceinline__ void had128_half(float (&v)[8], int hl)
+// 128-point Hadamard of one block held by 4 lanes x 32 consecutive values (element 32*hl + q): stages
+// w = 1 .. 16 inside the thread, then w = 32, 64 across lanes hl ^ 1, hl ^ 2 -- the same pairs and order
+// as the reference's had128 (ft_core.h:89-94) with 2 of the 7 stages on the shuffle unit
+__device__ __forceinline__ void had128_quad(float (&v)[32], int hl)
 {
 #pragma unroll
-    for (int w = 1; w < 8; w <<= 1)
+    for (int w = 1; w < 32; w <<= 1)
 #pragma unroll
-        for (int b = 0; b < 8; b += 2 * w)
+        for (int b = 0; b < 32; b += 2 * w)
 #pragma unroll
             for (int i = b; i < b + w; ++i) {
                 const float a = v[i], c = v[i + w];
@@ -74,10 +74,10 @@ __device__ __forceinline__ void had128_half(float (&v)[8], int hl)
                 v[i + w] = a - c;
             }
 #pragma unroll
-    for (int m = 1; m < 16; m <<= 1) {
+    for (int m = 1; m < 4; m <<= 1) {
         const bool upper = (hl & m) != 0;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < 32; ++q) {
             const float pv = __shfl_xor_sync(0xffffffffu, v[q], m);
             v[q] = upper ? (pv - v[q]) : (v[q] + pv);
         }
@@ -85,16 +85,16 @@ __device__ __forceinline__ void had128_half(float (&v)[8], int hl)
 }
 
 // one warp per sorted row p (rows p < *nrows; rows whose expert_sorted entry is negative are skipped):
-// half-warp h transforms 128-blocks 2j + h of the row for gate and up,
+// lanes 4g .. 4g+3 transform 128-block 8j + g of the row for gate and up,
 //   xt_{g,u}[p] = fp16(H128(fp16(x[token]) * suh_{g,u}) * 2^-3.5)
 // with 16-byte loads and stores; the row's indices are read once
 __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ XRows x, int x_dtype, const int* token_sorted,
                                                    const int* expert_sorted, const int* nrows,
                                                    const __half* w13_suh, int H, __half* xt_g, __half* xt_u)
 {
-    const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
+    const int lane = threadIdx.x & 31, hl = lane & 3, g = lane >> 2;
     const int nvalid = *nrows;
-    const int nb = H / 128, npair = (nb + 1) / 2;
+    const int nb = H / 128, nit = (nb + 7) / 8;
     const int wstride = gridDim.x * (blockDim.x >> 5);
     for (int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < nvalid; p += wstride) {
         const int e = expert_sorted[p];
@@ -108,25 +108,30 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ XRows
             row = (size_t)(t % x.per);
         }
         const __half* sg = w13_suh + (size_t)e * 2 * H;
-        __half* og = xt_g + (size_t)p * H;
-        __half* ou = xt_u + (size_t)p * H;
-#pragma unroll 2
-        for (int j = 0; j < npair; ++j) {
-            const int blk = 2 * j + half;
-            const bool act = blk < nb;   // an odd last block leaves the upper half-warp computing a copy
-            const int c = (act ? blk : blk - 1) * 128 + hl * 8;
-            float xv[8];
-            load8_as_half(xb, x_dtype, row * H + c, xv);
+        for (int j = 0; j < nit; ++j) {
+            const int blk = 8 * j + g;
+            const bool act = blk < nb;   // lanes past the last block transform a copy of block 0, unstored
+            const int c = (act ? blk : 0) * 128 + hl * 32;
 #pragma unroll
             for (int m = 0; m < 2; ++m) {
-                float s[8], v[8];
-                load8_half(sg + (size_t)m * H + c, s);
+                float v[32];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) v[q] = __fmul_rn(xv[q], s[q]);
-                had128_half(v, hl);
+                for (int k = 0; k < 4; ++k) {
+                    float xv[8], sv[8];
+                    load8_as_half(xb, x_dtype, row * H + c + 8 * k, xv);
+                    load8_half(sg + (size_t)m * H + c + 8 * k, sv);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) v[q] = __fmul_rn(v[q], kHad);
-                if (act) store8_half((m ? ou : og) + c, v);
+                    for (int q = 0; q < 8; ++q) v[8 * k + q] = __fmul_rn(xv[q], sv[q]);
+                }
+                had128_quad(v, hl);
+                __half* o = (m ? xt_u : xt_g) + (size_t)p * H + c;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    float w8[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) w8[q] = __fmul_rn(v[8 * k + q], kHad);
+                    if (act) store8_half(o + 8 * k, w8);
+                }
             }
         }
     }
