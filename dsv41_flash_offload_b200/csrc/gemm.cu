@@ -607,39 +607,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
 // ---------------------------------------------------------------------------------------------
 // CTA-pair kernel (tcgen05 cta_group::2, cluster of 2 CTAs on two SMs)
 //
-// One pair MMA (M = 256, N = 256, K = 16) takes rows 0-127 of A from CTA 0's shared memory and rows
-// 128-255 from CTA 1's, columns 0-127 of B from CTA 0 and 128-255 from CTA 1, and leaves each CTA's
-// 128 rows x 256 columns in that CTA's TMEM. Per SM this halves the operand bytes the tensor pipe reads
-// from shared memory for the same FLOPs (the single-CTA M=128 N=128 MMA reads ~120 B/cycle, nearly all
-// of the shared-memory bandwidth the decoders and TMA also need) and halves the activation bytes TMA
-// writes, while each SM still decodes 128 features per chunk.
-//   unit = (row pass, 256-feature block): gate/up passes of 256 rows (one pair M tile, both matrices
-//          in TMEM columns 0-255 / 256-511), down passes of 512 rows (two pair M tiles)
+// One pair MMA (M = 256, N = 128, K = 16) takes rows 0-127 of A from CTA 0's shared memory and rows
+// 128-255 from CTA 1's, columns 0-63 of B from CTA 0 and 64-127 from CTA 1, and leaves each CTA's 128
+// rows x 128 columns in that CTA's TMEM. Each decoded weight then serves 512 (gate/up) or 1024 (down)
+// rows while each SM decodes only 64 features per chunk: the decode, which bounds the single-CTA
+// kernel (measured: 64 tiles per SM per 64-k chunk take ~770 ns against ~570 ns of MMA), halves per
+// SM for the same MMA work.
+//   unit = (row pass, 128-feature block): gate/up passes of 512 rows (two pair M tiles x two matrices
+//          in the 512 TMEM columns), down passes of 1024 rows (four pair M tiles)
 //   CTA r: its 128-row halves of A (TMA, signalling CTA 0's full barrier), the trellis of features
-//          block*256 + 128r .. +127 (its own T ring), decoded by its 8 decoder warps into its B stage
-//          (arrival on CTA 0's full barrier), and the epilogue of its own 128 rows
-//   CTA 0: warps 1 and 3 issue the pair MMAs (one accumulator each) and commit every stage to the
-//          empty barrier of both CTAs (two commits, no multicast form)
-// Stages: 3 (gate/up) or 4 (down) of A + B, so the decoders run up to two chunks ahead of the MMAs.
+//          block*128 + 64r .. +63 (its own T ring), decoded by its 8 decoder warps into its B stage
+//          (arrival on CTA 0's full barrier), and the epilogue of its own rows
+//   CTA 0: warps 1 and 3 issue the pair MMAs (accumulators alternate between them) and commit every
+//          stage to the empty barrier of both CTAs (two commits, no multicast form)
+// Two stages of A + B (80 KB / 72 KB), an 8-stage trellis ring.
 // ---------------------------------------------------------------------------------------------
 #ifndef DSV41_GEMM_PAIR
 #define DSV41_GEMM_PAIR 0
 #endif
-constexpr int kPairM = 2 * kBM;   // rows per pair M tile
-constexpr int kPairN = 2 * kBN;   // features per unit
+constexpr int kPairM = 2 * kBM;    // rows per pair M tile (128 per CTA)
+constexpr int kPairN = kBN;        // features per unit
+constexpr int kCtaN = kPairN / 2;  // features of B decoded by each CTA
 constexpr uint32_t kIdescPair = (1u << 4) | ((uint32_t)(kPairN >> 3) << 17) | ((uint32_t)(kPairM >> 4) << 24);
 
 template <int MODE, int K>
 struct PairCfg {
-    static_assert(kBK == 64, "the pair kernel uses 64-k chunks");
     static constexpr int nmat = MODE == 0 ? 2 : 1;
-    static constexpr int pmt = MODE == 0 ? 1 : 2;      // pair M tiles per pass
-    static constexpr int rows_per_pass = pmt * kPairM;
-    static constexpr int a_bytes = nmat * pmt * kTileA; // this CTA's 128-row halves
-    static constexpr int b_bytes = nmat * kTileB;       // this CTA's 128 decoded features
-    static constexpr int stages = MODE == 0 ? 3 : 4;
-    static constexpr int t_bytes = nmat * kKT * tr_row<K>();
-    static constexpr int t_stages = MODE == 0 ? 4 : 8;
+    static constexpr int pmt = MODE == 0 ? 2 : 4;           // pair M tiles per pass
+    static constexpr int rows_per_pass = pmt * kPairM;       // 512 / 1024
+    static constexpr int a_bytes = nmat * pmt * kTileA;      // this CTA's 128-row halves
+    static constexpr int b_bytes = nmat * kCtaN * kRowB;     // this CTA's 64 decoded features
+    static constexpr int stages = 2 * (64 / kBK);
+    static constexpr int ntiles = kCtaN / 16;                // n-tiles per k-tile row and CTA
+    static constexpr int t_row = ntiles * TileFmt<K>::bytes;
+    static constexpr int t_bytes = nmat * kKT * t_row;
+    static constexpr int t_stages = 8 * (64 / kBK);
     static constexpr int a_off = 0;
     static constexpr int b_off = a_off + stages * a_bytes;
     static constexpr int t_off = b_off + stages * b_bytes;
@@ -647,7 +649,7 @@ struct PairCfg {
     static constexpr int n_bars = 2 * stages + 2 * t_stages + 1;
     static constexpr int smem_bytes = bar_off + 1024 /* align */ + n_bars * 8 + 16;
     static_assert(smem_bytes <= 232448, "shared memory over the 227 KB per-block limit");
-    static_assert(rows_per_pass == GemmCfg<MODE, K>::rows_per_pass, "one plan serves both kernels");
+    static_assert(pmt * nmat * kPairN <= 512, "accumulators exceed the 512 TMEM columns");
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank()
@@ -713,7 +715,6 @@ template <int MODE, int K>
 __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_pair_kernel(const __grid_constant__ GemmParams p)
 {
     using Cfg = PairCfg<MODE, K>;
-    constexpr int kTrRow = tr_row<K>();
     constexpr int S = Cfg::stages, TS = Cfg::t_stages;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_addr(smem_raw);
@@ -766,8 +767,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_pair_kernel(const _
     const uint32_t tmem = *tmem_slot;
 
     auto stage_a = [&](int s, int mat, int pm) { return smem + Cfg::a_off + s * Cfg::a_bytes + (mat * Cfg::pmt + pm) * kTileA; };
-    auto stage_b = [&](int s, int mat) { return smem + Cfg::b_off + s * Cfg::b_bytes + mat * kTileB; };
-    auto stage_t = [&](int s, int mat, int kt) { return smem + Cfg::t_off + s * Cfg::t_bytes + (mat * kKT + kt) * kTrRow; };
+    auto stage_b = [&](int s, int mat) { return smem + Cfg::b_off + s * Cfg::b_bytes + mat * (kCtaN * kRowB); };
+    auto stage_t = [&](int s, int mat, int kt) { return smem + Cfg::t_off + s * Cfg::t_bytes + (mat * kKT + kt) * Cfg::t_row; };
     // half (pm, r) of a pass holds rows pm*256 + 128r .. +127
     auto half_active = [](int rows, int pm, int r) { return rows > pm * kPairM + r * kBM; };
 
@@ -818,7 +819,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_pair_kernel(const _
             if (!lact || u >= n_units) return nullptr;
             const int e = p.passes[u / n_fb].x, fb = u % n_fb;
             const int64_t base = lmat ? p.tab_b[e] : p.tab_a[e];
-            return reinterpret_cast<const uint8_t*>(base) + (size_t)(fb * 16 + (int)rank * 8) * TileFmt<K>::bytes;
+            return reinterpret_cast<const uint8_t*>(base) + (size_t)(fb * (kPairN / 16) + (int)rank * Cfg::ntiles) * TileFmt<K>::bytes;
         };
         const size_t chunk_stride = (size_t)kKT * ntile_row * TileFmt<K>::bytes;
         const size_t lane_off = (size_t)lkt * ntile_row * TileFmt<K>::bytes;
@@ -826,7 +827,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_pair_kernel(const _
         const uint8_t* cur = unit_base(pair);
         const uint8_t* nxt = unit_base(pair + n_pairs);
         for (int c = 0; c < kTrPrefetch && c < n_chunks; ++c)
-            if (cur) l2_prefetch_bulk(cur + c * chunk_stride + lane_off, kTrRow);
+            if (cur) l2_prefetch_bulk(cur + c * chunk_stride + lane_off, Cfg::t_row);
         for (int u = pair; u < n_units && ok; u += n_pairs) {
             for (int c = 0; c < n_chunks; ++c, ++it) {
                 const int s = it % TS;
@@ -834,7 +835,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_pair_kernel(const _
                     const int cp = c + kTrPrefetch;
                     const uint8_t* q = cp < n_chunks ? cur : nxt;
                     const int cq = cp < n_chunks ? cp : cp - n_chunks;
-                    if (q && cq < n_chunks) l2_prefetch_bulk(q + cq * chunk_stride + lane_off, kTrRow);
+                    if (q && cq < n_chunks) l2_prefetch_bulk(q + cq * chunk_stride + lane_off, Cfg::t_row);
                 }
                 if (!mbar_wait_bounded(&t_empty[s], ((it / TS) & 1) ^ 1, abort_flag, p.status)) {
                     ok = false;
@@ -842,7 +843,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_pair_kernel(const _
                 }
                 if (lane == 0) mbar_arrive_expect_tx(&t_full[s], Cfg::t_bytes);
                 __syncwarp();
-                if (lact) bulk_g2s(stage_t(s, lmat, lkt), cur + c * chunk_stride + lane_off, kTrRow, &t_full[s], pol);
+                if (lact) bulk_g2s(stage_t(s, lmat, lkt), cur + c * chunk_stride + lane_off, Cfg::t_row, &t_full[s], pol);
             }
             cur = nxt;
             nxt = unit_base(u + 2 * n_pairs);
@@ -880,11 +881,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_pair_kernel(const _
                     for (int pm = 0; pm < Cfg::pmt; ++pm) {
 #pragma unroll
                         for (int mat = 0; mat < Cfg::nmat; ++mat) {
-                            const int acc = pm * Cfg::nmat + mat;   // 0 or 1: one accumulator per issuer
-                            if (acc != me || pm * kPairM >= rows) continue;
+                            const int acc = pm * Cfg::nmat + mat;   // accumulators alternate between the issuers
+                            if ((acc & 1) != me || pm * kPairM >= rows) continue;
                             const uint32_t d = tmem + (uint32_t)(acc * kPairN);
                             const uint64_t ad = ad_s + (uint64_t)(((mat * Cfg::pmt + pm) * kTileA) >> 4);
-                            const uint64_t bd = bd_s + (uint64_t)((mat * kTileB) >> 4);
+                            const uint64_t bd = bd_s + (uint64_t)((mat * kCtaN * kRowB) >> 4);
 #pragma unroll
                             for (int kk = 0; kk < kBK / 16; ++kk) umma_f16_pair(d, ad + 2 * kk, bd + 2 * kk, kk ? 1u : acc0);
                         }
@@ -918,7 +919,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_pair_kernel(const _
         const uint32_t k16 = p.k16;
         const int r0 = (lane & 3) * 2, c0 = lane >> 2;
         constexpr int wpg = kDecWarps / (Cfg::nmat * kKT);
-        constexpr int ntn = 8 / wpg;
+        constexpr int ntn = Cfg::ntiles / wpg;
         const int grp = d / wpg;
         const int dmat = grp / kKT, dkt = grp % kKT;
         const int nt0 = (d % wpg) * ntn;
@@ -927,10 +928,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_pair_kernel(const _
         for (int q = 0; q < 4; ++q) {
             const int n = c0 + ((q >> 1) << 3);
             const int k = dkt * 16 + r0 + ((q & 1) << 3);
-            boff[q] = (uint32_t)((n >> 3) * kAtom + (n & 7) * kRowB + (((k >> 3) ^ (n & 7)) * 16) + (k & 7) * 2);
+            const int sw = kBK == 64 ? (n & 7) : ((n & 7) >> 1);
+            boff[q] = (uint32_t)((n >> 3) * kAtom + (n & 7) * kRowB + (((k >> 3) ^ sw) * 16) + (k & 7) * 2);
         }
         const int quarter = warp & 3;                 // TMEM lanes this warp may access
-        const int half = d >> 2;                      // epilogue: feature half (gate/up) or pair M tile (down)
+        const int half = d >> 2;                      // epilogue: which half of the pass's pair M tiles
         uint32_t it = 0, ib = 0, units_done = 0;
         bool ok = true;
         for (int u = pair; u < n_units && ok; u += n_pairs, ++units_done) {
@@ -973,54 +975,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_pair_kernel(const _
             }
             tc_fence_after();
             const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-            if (MODE == 0) {
-                // this warp: rows 128*rank + 32*quarter + lane, features fb*256 + half*128 .. +127
-                const int row = (int)rank * kBM + quarter * 32 + lane;
-                if ((int)rank * kBM + quarter * 32 < rows) {   // warp-uniform: some row of the warp exists
-                    const int f0 = fb * kPairN + half * kBN;
-                    const uint32_t colg = (uint32_t)(half * kBN), colu = (uint32_t)(kPairN + half * kBN);
-                    const __half* svg = p.svh_a + (size_t)e * 2 * p.N + f0;
-                    float v[128];
-                    gateup_epilogue(v, lane_addr + colg, lane_addr + colu, svg, svg + p.N,
-                                    p.suh_d + (size_t)e * p.N + f0, p.limit);
-                    if (row < rows) {
-                        uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(row0 + row) * p.N + f0);
-#pragma unroll
-                        for (int c8 = 0; c8 < 16; ++c8) {
-                            uint4 o;
-                            o.x = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 0], v[c8 * 8 + 1]));
-                            o.y = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 2], v[c8 * 8 + 3]));
-                            o.z = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 4], v[c8 * 8 + 5]));
-                            o.w = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 6], v[c8 * 8 + 7]));
-                            dst[c8] = o;
-                        }
-                    }
-                }
-            } else {
-                // this warp: pair M tile pm = half, rows pm*256 + 128*rank + 32*quarter + lane, all 256 features
-                const int pm = half;
+            const int f0 = fb * kPairN;   // the unit's 128 features: TMEM column j is feature f0 + j
+#pragma unroll 1
+            for (int ei = 0; ei < Cfg::pmt / 2; ++ei) {
+                // this warp: pair M tile pm, rows pm*256 + 128*rank + 32*quarter + lane
+                const int pm = half * (Cfg::pmt / 2) + ei;
                 const int rbase = pm * kPairM + (int)rank * kBM + quarter * 32;
                 const int row = rbase + lane;
-                if (rbase < rows) {
-#pragma unroll 1
-                    for (int blk = 0; blk < 2; ++blk) {
-                        const uint32_t col = (uint32_t)(pm * kPairN + blk * kBN);
-                        const int f0 = fb * kPairN + blk * kBN;
-                        float v[128];
-                        tmem_ld128(lane_addr + col, v);
-                        out_block128(v, p.svh_a + (size_t)e * p.N + f0);
-                        if (row < rows) {
-                            uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(row0 + row) * p.N + f0);
+                if (rbase >= rows) continue;   // warp-uniform: no row of this warp exists
+                float v[128];
+                if (MODE == 0) {
+                    const __half* svg = p.svh_a + (size_t)e * 2 * p.N + f0;
+                    gateup_epilogue(v, lane_addr + (uint32_t)(pm * 2 * kPairN), lane_addr + (uint32_t)((pm * 2 + 1) * kPairN),
+                                    svg, svg + p.N, p.suh_d + (size_t)e * p.N + f0, p.limit);
+                } else {
+                    tmem_ld128(lane_addr + (uint32_t)(pm * kPairN), v);
+                    out_block128(v, p.svh_a + (size_t)e * p.N + f0);
+                }
+                if (row < rows) {
+                    uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(row0 + row) * p.N + f0);
 #pragma unroll
-                            for (int c8 = 0; c8 < 16; ++c8) {
-                                uint4 o;
-                                o.x = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 0], v[c8 * 8 + 1]));
-                                o.y = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 2], v[c8 * 8 + 3]));
-                                o.z = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 4], v[c8 * 8 + 5]));
-                                o.w = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 6], v[c8 * 8 + 7]));
-                                dst[c8] = o;
-                            }
-                        }
+                    for (int c8 = 0; c8 < 16; ++c8) {
+                        uint4 o;
+                        o.x = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 0], v[c8 * 8 + 1]));
+                        o.y = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 2], v[c8 * 8 + 3]));
+                        o.z = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 4], v[c8 * 8 + 5]));
+                        o.w = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 6], v[c8 * 8 + 7]));
+                        dst[c8] = o;
                     }
                 }
             }
@@ -1039,17 +1020,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_pair_kernel(const _
 // plan: row passes of the busy experts (gate/up 256 rows, down 512 rows)
 // ---------------------------------------------------------------------------------------------
 __global__ void gemm_plan_kernel(const int* fat_experts, const int* n_fat, const int* counts, const int* offsets,
-                                 int4* passes0, int* n0, int4* passes1, int* n1)
+                                 int rp0, int rp1, int4* passes0, int* n0, int4* passes1, int* n1)
 {
     if (threadIdx.x != 0) return;
     const int nf = *n_fat;
     int a = 0, b = 0;
     for (int i = 0; i < nf; ++i) {
         const int e = fat_experts[i], R = counts[e], r0 = offsets[e];
-        for (int r = 0; r < R; r += GemmCfg<0, 3>::rows_per_pass)
-            passes0[a++] = make_int4(e, r0 + r, min(GemmCfg<0, 3>::rows_per_pass, R - r), 0);
-        for (int r = 0; r < R; r += GemmCfg<1, 3>::rows_per_pass)
-            passes1[b++] = make_int4(e, r0 + r, min(GemmCfg<1, 3>::rows_per_pass, R - r), 0);
+        for (int r = 0; r < R; r += rp0) passes0[a++] = make_int4(e, r0 + r, min(rp0, R - r), 0);
+        for (int r = 0; r < R; r += rp1) passes1[b++] = make_int4(e, r0 + r, min(rp1, R - r), 0);
     }
     *n0 = a;
     *n1 = b;
@@ -1136,7 +1115,9 @@ static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
     int* counters = reinterpret_cast<int*>(a.scratch);
     cudaError_t err;
     if (MODE == 0) {
-        gemm_plan_kernel<<<1, 32, 0, st>>>(a.fat_experts, a.n_fat, a.counts, a.offsets, passes0, counters, passes1,
+        const int rp0 = DSV41_GEMM_PAIR ? PairCfg<0, K>::rows_per_pass : GemmCfg<0, K>::rows_per_pass;
+        const int rp1 = DSV41_GEMM_PAIR ? PairCfg<1, K>::rows_per_pass : GemmCfg<1, K>::rows_per_pass;
+        gemm_plan_kernel<<<1, 32, 0, st>>>(a.fat_experts, a.n_fat, a.counts, a.offsets, rp0, rp1, passes0, counters, passes1,
                                            counters + 1);
         if ((err = cudaGetLastError()) != cudaSuccess) return err;
     }
@@ -1169,7 +1150,8 @@ static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
     p.status = a.status;
     p.limit = a.limit;
     p.k16 = 65536u;
-    if (DSV41_GEMM_PAIR) return launch_pair<MODE, K>(p, max_passes(N, E, Cfg::rows_per_pass) * (p.N / kPairN), st);
+    if (DSV41_GEMM_PAIR)
+        return launch_pair<MODE, K>(p, max_passes(N, E, PairCfg<MODE, K>::rows_per_pass) * (p.N / kPairN), st);
     const size_t smem = Cfg::smem_bytes;
     if ((err = cudaFuncSetAttribute((const void*)exl3_gemm_kernel<MODE, K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)smem)) != cudaSuccess)
