@@ -290,27 +290,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar)
 {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
-#ifndef DSV41_MBAR_TEST_WAIT
-#define DSV41_MBAR_TEST_WAIT 0
-#endif
-// one probe of phase `parity`: try_wait may suspend the thread for a while before answering false;
-// test_wait (DSV41_MBAR_TEST_WAIT) answers at once
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
 {
     uint32_t ok;
-#if DSV41_MBAR_TEST_WAIT
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-#else
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
         : "r"(smem_addr(bar)), "r"(parity)
         : "memory");
-#endif
     return ok != 0;
 }
 __device__ __forceinline__ uint64_t globaltimer_ns()

@@ -39,13 +39,8 @@ constexpr int kWarpMma = 1;      // TMEM allocator + single-thread tcgen05.mma i
 constexpr int kWarpT = 2;        // bulk-copy producer of the trellis k-rows
 constexpr int kWarpMma2 = 3;     // second MMA issuer (merged ring)
 constexpr int kWarpDec0 = 4;     // warps 4..11: decoders, then epilogue
-#ifndef DSV41_GEMM_DEC_WARPS
-#define DSV41_GEMM_DEC_WARPS 8
-#endif
-constexpr int kDecWarps = DSV41_GEMM_DEC_WARPS;           // 8 or 16 decoders
-constexpr int kEpiWarps = 8;                              // the first 8 decoders also run the epilogue
-constexpr int kGemmThreads = (kWarpDec0 + kDecWarps) * 32;
-static_assert(kDecWarps == 8 || kDecWarps == 16, "decoder warps: 8 or 16");
+constexpr int kDecWarps = 8;
+constexpr int kGemmThreads = (kWarpDec0 + kDecWarps) * 32;   // 384
 #ifndef DSV41_GEMM_DEC_UNROLL
 #define DSV41_GEMM_DEC_UNROLL 4
 #endif
@@ -503,7 +498,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
         __syncwarp();
     } else if (warp >= kWarpDec0) {
         // ------------------------------- decoders + epilogue -------------------------------
-        const int d = warp - kWarpDec0;               // 0 .. kDecWarps-1
+        const int d = warp - kWarpDec0;               // 0..7
         const LaneDec<K> lw = lane_dec_setup<K>(lane);
         const uint32_t k16 = p.k16;
         const int r0 = (lane & 3) * 2, c0 = lane >> 2;
@@ -558,7 +553,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 }
             }
             if (!ok) break;
-            if (d >= kEpiWarps) continue;   // decode-only warp: on to the next unit's chunks
             // ------------------------------- epilogue -------------------------------
             if (!mbar_wait_bounded(acc_full, units_done & 1, abort_flag, p.status)) {
                 ok = false;
@@ -601,418 +595,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
     if (warp == kWarpMma) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
-    }
-}
-
-// ---------------------------------------------------------------------------------------------
-// CTA-pair kernel (tcgen05 cta_group::2, cluster of 2 CTAs on two SMs)
-//
-// One pair MMA (M = 256, N = 128, K = 16) takes rows 0-127 of A from CTA 0's shared memory and rows
-// 128-255 from CTA 1's, columns 0-63 of B from CTA 0 and 64-127 from CTA 1, and leaves each CTA's 128
-// rows x 128 columns in that CTA's TMEM. Each decoded weight then serves 512 (gate/up) or 1024 (down)
-// rows while each SM decodes only 64 features per chunk: the decode, which bounds the single-CTA
-// kernel (measured: 64 tiles per SM per 64-k chunk take ~770 ns against ~570 ns of MMA), halves per
-// SM for the same MMA work.
-//   unit = (row pass, 128-feature block): gate/up passes of 512 rows (two pair M tiles x two matrices
-//          in the 512 TMEM columns), down passes of 1024 rows (four pair M tiles)
-//   CTA r: its 128-row halves of A (TMA, signalling CTA 0's full barrier), the trellis of features
-//          block*128 + 64r .. +63 (its own T ring), decoded by its 8 decoder warps into its B stage
-//          (arrival on CTA 0's full barrier), and the epilogue of its own rows
-//   CTA 0: warps 1 and 3 issue the pair MMAs (accumulators alternate between them) and commit every
-//          stage to the empty barrier of both CTAs (two commits, no multicast form)
-// Two stages of A + B (80 KB / 72 KB), an 8-stage trellis ring.
-// ---------------------------------------------------------------------------------------------
-#ifndef DSV41_GEMM_PAIR
-#define DSV41_GEMM_PAIR 0
-#endif
-constexpr int kPairM = 2 * kBM;    // rows per pair M tile (128 per CTA)
-constexpr int kPairN = kBN;        // features per unit
-constexpr int kCtaN = kPairN / 2;  // features of B decoded by each CTA
-constexpr uint32_t kIdescPair = (1u << 4) | ((uint32_t)(kPairN >> 3) << 17) | ((uint32_t)(kPairM >> 4) << 24);
-
-template <int MODE, int K>
-struct PairCfg {
-    static constexpr int nmat = MODE == 0 ? 2 : 1;
-    static constexpr int pmt = MODE == 0 ? 2 : 4;           // pair M tiles per pass
-    static constexpr int rows_per_pass = pmt * kPairM;       // 512 / 1024
-    static constexpr int a_bytes = nmat * pmt * kTileA;      // this CTA's 128-row halves
-    static constexpr int b_bytes = nmat * kCtaN * kRowB;     // this CTA's 64 decoded features
-    static constexpr int stages = 2 * (64 / kBK);
-    static constexpr int ntiles = kCtaN / 16;                // n-tiles per k-tile row and CTA
-    static constexpr int t_row = ntiles * TileFmt<K>::bytes;
-    static constexpr int t_bytes = nmat * kKT * t_row;
-    static constexpr int t_stages = 8 * (64 / kBK);
-    static constexpr int a_off = 0;
-    static constexpr int b_off = a_off + stages * a_bytes;
-    static constexpr int t_off = b_off + stages * b_bytes;
-    static constexpr int bar_off = t_off + t_stages * t_bytes;   // multiple of 1024
-    static constexpr int n_bars = 2 * stages + 2 * t_stages + 1;
-    static constexpr int smem_bytes = bar_off + 1024 /* align */ + n_bars * 8 + 16;
-    static_assert(smem_bytes <= 232448, "shared memory over the 227 KB per-block limit");
-    static_assert(pmt * nmat * kPairN <= 512, "accumulators exceed the 512 TMEM columns");
-};
-
-__device__ __forceinline__ uint32_t cluster_ctarank()
-{
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t cluster_idx()
-{
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t cluster_count()
-{
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-    return r;
-}
-// shared::cluster address of the same shared-memory location in CTA `rank` of this cluster
-__device__ __forceinline__ uint32_t mapa_rank(const void* p, uint32_t rank)
-{
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ void cluster_sync_all()
-{
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// arrival on a barrier of the other CTA (default .release.cta semantics: the writer fences its shared-memory
-// stores to the async proxy first; a .cluster-scope release costs a memory barrier per arrival)
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr)
-{
-    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate)
-{
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(kIdescPair), "r"(accumulate)
-        : "memory");
-}
-// arrive on the mbarrier at `cluster_addr` (either CTA of the pair) once this thread's pair MMAs finish
-__device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr)
-{
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_addr)
-                 : "memory");
-}
-// TMA tile load into this CTA's shared memory whose completion is counted on CTA 0's barrier
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* tm, int c0, int c1, uint32_t leader_bar)
-{
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-        "[%4];" ::"r"(smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(leader_bar)
-        : "memory");
-}
-
-template <int MODE, int K>
-__global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_pair_kernel(const __grid_constant__ GemmParams p)
-{
-    using Cfg = PairCfg<MODE, K>;
-    constexpr int S = Cfg::stages, TS = Cfg::t_stages;
-    extern __shared__ uint8_t smem_raw[];
-    const uint32_t raw = smem_addr(smem_raw);
-    uint8_t* smem = smem_raw + ((1024 - (raw & 1023)) & 1023);   // same offset in both CTAs
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::bar_off);
-    uint64_t* full = bars;             // CTA 0: TMA bytes of both CTAs + 16 decoder-warp arrivals
-    uint64_t* empty = full + S;        // both CTAs: the two issuers' commits
-    uint64_t* t_full = empty + S;
-    uint64_t* t_empty = t_full + TS;
-    uint64_t* acc_full = t_empty + TS; // both CTAs: the two issuers' commits after a unit's last chunk
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + Cfg::n_bars);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Cfg::n_bars) + 1;
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t rank = cluster_ctarank();
-    const int pair = (int)cluster_idx(), n_pairs = (int)cluster_count();
-    const int n_fb = p.N / kPairN;
-    const int n_chunks = p.K / kBK;
-    const int n_units = (*p.n_passes) * n_fb;
-    const int ntile_row = p.N / 16;
-    // no busy expert for this pair (the usual decode case): both CTAs leave before any cluster traffic
-    if (n_units <= pair) return;
-    int my_units = 0;
-    for (int u = pair; u < n_units; u += n_pairs) ++my_units;
-    const uint32_t total_chunks = (uint32_t)my_units * (uint32_t)n_chunks;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1 + 2 * kDecWarps);
-            mbar_init(&empty[s], 2);
-        }
-        for (int s = 0; s < TS; ++s) {
-            mbar_init(&t_full[s], 1);
-            mbar_init(&t_empty[s], kDecWarps);
-        }
-        mbar_init(acc_full, 2);
-        *abort_flag = 0;
-        fence_mbar_init();
-    }
-    __syncthreads();
-    cluster_sync_all();   // both CTAs' barriers initialised before any remote arrival
-    if (warp == kWarpMma) {
-        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_addr(tmem_slot))
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-
-    auto stage_a = [&](int s, int mat, int pm) { return smem + Cfg::a_off + s * Cfg::a_bytes + (mat * Cfg::pmt + pm) * kTileA; };
-    auto stage_b = [&](int s, int mat) { return smem + Cfg::b_off + s * Cfg::b_bytes + mat * (kCtaN * kRowB); };
-    auto stage_t = [&](int s, int mat, int kt) { return smem + Cfg::t_off + s * Cfg::t_bytes + (mat * kKT + kt) * Cfg::t_row; };
-    // half (pm, r) of a pass holds rows pm*256 + 128r .. +127
-    auto half_active = [](int rows, int pm, int r) { return rows > pm * kPairM + r * kBM; };
-
-    if (warp == kWarpA) {
-        // ------------------------------ activation producer (both CTAs) ------------------------------
-        uint32_t it = 0;
-        bool ok = true;
-        if (lane == 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_a)) : "memory");
-            if (MODE == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.tm_b)) : "memory");
-            for (int u = pair; u < n_units && ok; u += n_pairs) {
-                const int4 P = p.passes[u / n_fb];
-                const int row0 = P.y, rows = P.z;
-                int halves = 0;
-                for (int pm = 0; pm < Cfg::pmt; ++pm) halves += half_active(rows, pm, 0) + half_active(rows, pm, 1);
-                for (int c = 0; c < n_chunks; ++c, ++it) {
-                    const int s = it % S;
-                    if (!mbar_wait_bounded(&empty[s], ((it / S) & 1) ^ 1, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    if (rank == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(Cfg::nmat * halves * kTileA));
-                    const uint32_t leader_full = mapa_rank(&full[s], 0);
-                    for (int mat = 0; mat < Cfg::nmat; ++mat)
-                        for (int pm = 0; pm < Cfg::pmt; ++pm)
-                            if (half_active(rows, pm, (int)rank))
-                                tma_load_2d_pair(stage_a(s, mat, pm), mat ? &p.tm_b : &p.tm_a, c * kBK,
-                                                 row0 + pm * kPairM + (int)rank * kBM, leader_full);
-                }
-            }
-            if (!ok) {
-                // copies already issued complete on CTA 0's barrier; give them time to land before exit
-                const uint64_t t0 = globaltimer_ns();
-                while (globaltimer_ns() - t0 < 1000000ull) {}
-            }
-        }
-        __syncwarp();
-    } else if (warp == kWarpT) {
-        // ------------------------------ trellis producer (both CTAs, own ring) ------------------------------
-        uint32_t it = 0;
-        bool ok = true;
-        const uint64_t pol = l2_policy_evict_first();
-        // this CTA's 8 n-tiles of the 16 in a 256-feature block; per-unit bases resolved once per unit
-        // (the per-chunk loop only adds offsets, as in the single-CTA kernel)
-        const bool lact = lane < Cfg::nmat * kKT;
-        const int lmat = lane / kKT, lkt = lane % kKT;
-        auto unit_base = [&](int u) -> const uint8_t* {
-            if (!lact || u >= n_units) return nullptr;
-            const int e = p.passes[u / n_fb].x, fb = u % n_fb;
-            const int64_t base = lmat ? p.tab_b[e] : p.tab_a[e];
-            return reinterpret_cast<const uint8_t*>(base) + (size_t)(fb * (kPairN / 16) + (int)rank * Cfg::ntiles) * TileFmt<K>::bytes;
-        };
-        const size_t chunk_stride = (size_t)kKT * ntile_row * TileFmt<K>::bytes;
-        const size_t lane_off = (size_t)lkt * ntile_row * TileFmt<K>::bytes;
-        constexpr int kTrPrefetch = 16;
-        const uint8_t* cur = unit_base(pair);
-        const uint8_t* nxt = unit_base(pair + n_pairs);
-        for (int c = 0; c < kTrPrefetch && c < n_chunks; ++c)
-            if (cur) l2_prefetch_bulk(cur + c * chunk_stride + lane_off, Cfg::t_row);
-        for (int u = pair; u < n_units && ok; u += n_pairs) {
-            for (int c = 0; c < n_chunks; ++c, ++it) {
-                const int s = it % TS;
-                {
-                    const int cp = c + kTrPrefetch;
-                    const uint8_t* q = cp < n_chunks ? cur : nxt;
-                    const int cq = cp < n_chunks ? cp : cp - n_chunks;
-                    if (q && cq < n_chunks) l2_prefetch_bulk(q + cq * chunk_stride + lane_off, Cfg::t_row);
-                }
-                if (!mbar_wait_bounded(&t_empty[s], ((it / TS) & 1) ^ 1, abort_flag, p.status)) {
-                    ok = false;
-                    break;
-                }
-                if (lane == 0) mbar_arrive_expect_tx(&t_full[s], Cfg::t_bytes);
-                __syncwarp();
-                if (lact) bulk_g2s(stage_t(s, lmat, lkt), cur + c * chunk_stride + lane_off, Cfg::t_row, &t_full[s], pol);
-            }
-            cur = nxt;
-            nxt = unit_base(u + 2 * n_pairs);
-        }
-        if (!ok && lane == 0) {
-            for (uint32_t q = 1; q <= (it < (uint32_t)TS ? it : (uint32_t)TS); ++q) {
-                const uint32_t j = it - q;
-                const uint64_t t0 = globaltimer_ns();
-                while (!mbar_try_wait(&t_full[j % TS], (j / TS) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {}
-            }
-        }
-        __syncwarp();
-    } else if (warp == kWarpMma || warp == kWarpMma2) {
-        // --------------------------- pair MMA issuers (CTA 0, one thread each) ---------------------------
-        const int me = warp == kWarpMma ? 0 : 1;
-        if (lane == 0 && rank == 0) {
-            uint32_t ib = 0;
-            bool ok = true;
-            const uint64_t adesc0 = sw_desc(smem_addr(smem + Cfg::a_off));
-            const uint64_t bdesc0 = sw_desc(smem_addr(smem + Cfg::b_off));
-            const uint32_t peer_acc = mapa_rank(acc_full, 1);
-            for (int u = pair; u < n_units && ok; u += n_pairs) {
-                const int rows = p.passes[u / n_fb].z;
-                for (int c = 0; c < n_chunks; ++c, ++ib) {
-                    const int s = ib % S;
-                    if (!mbar_wait_bounded(&full[s], (ib / S) & 1, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint64_t ad_s = adesc0 + (uint64_t)((s * Cfg::a_bytes) >> 4);
-                    const uint64_t bd_s = bdesc0 + (uint64_t)((s * Cfg::b_bytes) >> 4);
-                    const uint32_t acc0 = c > 0 ? 1u : 0u;
-#pragma unroll
-                    for (int pm = 0; pm < Cfg::pmt; ++pm) {
-#pragma unroll
-                        for (int mat = 0; mat < Cfg::nmat; ++mat) {
-                            const int acc = pm * Cfg::nmat + mat;   // accumulators alternate between the issuers
-                            if ((acc & 1) != me || pm * kPairM >= rows) continue;
-                            const uint32_t d = tmem + (uint32_t)(acc * kPairN);
-                            const uint64_t ad = ad_s + (uint64_t)(((mat * Cfg::pmt + pm) * kTileA) >> 4);
-                            const uint64_t bd = bd_s + (uint64_t)((mat * kCtaN * kRowB) >> 4);
-#pragma unroll
-                            for (int kk = 0; kk < kBK / 16; ++kk) umma_f16_pair(d, ad + 2 * kk, bd + 2 * kk, kk ? 1u : acc0);
-                        }
-                    }
-                    // releases stage s in both CTAs once this thread's MMAs so far have finished
-                    umma_commit_pair(smem_addr(&empty[s]));
-                    umma_commit_pair(mapa_rank(&empty[s], 1));
-                }
-                if (ok) {
-                    umma_commit_pair(smem_addr(acc_full));
-                    umma_commit_pair(peer_acc);
-                }
-            }
-            // the last MMAs must finish before TMEM is released (and before CTA 1 may leave)
-            if (ib > 0) {
-                const uint32_t j = ib - 1;
-                const uint64_t t0 = globaltimer_ns();
-                while (!mbar_try_wait(&empty[j % S], (j / S) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {}
-            }
-        } else if (lane == 0 && rank == 1 && me == 0 && total_chunks > 0) {
-            // CTA 1 receives CTA 0's commits: wait for the last one before this CTA may leave
-            const uint32_t j = total_chunks - 1;
-            const uint64_t t0 = globaltimer_ns();
-            while (!mbar_try_wait(&empty[j % S], (j / S) & 1) && globaltimer_ns() - t0 < kWaitLimitNs) {}
-        }
-        __syncwarp();
-    } else if (warp >= kWarpDec0) {
-        // ------------------------------- decoders + epilogue (both CTAs) -------------------------------
-        const int d = warp - kWarpDec0;               // 0 .. kDecWarps-1
-        const LaneDec<K> lw = lane_dec_setup<K>(lane);
-        const uint32_t k16 = p.k16;
-        const int r0 = (lane & 3) * 2, c0 = lane >> 2;
-        constexpr int wpg = kDecWarps / (Cfg::nmat * kKT);
-        constexpr int ntn = Cfg::ntiles / wpg;
-        const int grp = d / wpg;
-        const int dmat = grp / kKT, dkt = grp % kKT;
-        const int nt0 = (d % wpg) * ntn;
-        uint32_t boff[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int n = c0 + ((q >> 1) << 3);
-            const int k = dkt * 16 + r0 + ((q & 1) << 3);
-            const int sw = kBK == 64 ? (n & 7) : ((n & 7) >> 1);
-            boff[q] = (uint32_t)((n >> 3) * kAtom + (n & 7) * kRowB + (((k >> 3) ^ sw) * 16) + (k & 7) * 2);
-        }
-        const int quarter = warp & 3;                 // TMEM lanes this warp may access
-        const int half = d >> 2;                      // epilogue: which half of the pass's pair M tiles
-        uint32_t it = 0, ib = 0, units_done = 0;
-        bool ok = true;
-        for (int u = pair; u < n_units && ok; u += n_pairs, ++units_done) {
-            const int fb = u % n_fb;
-            const int4 P = p.passes[u / n_fb];
-            const int e = P.x, row0 = P.y, rows = P.z;
-            for (int c = 0; c < n_chunks; ++c, ++it, ++ib) {
-                const int st = it % TS, sb = ib % S;
-                if (!mbar_wait_bounded(&t_full[st], (it / TS) & 1, abort_flag, p.status) ||
-                    !mbar_wait_bounded(&empty[sb], ((ib / S) & 1) ^ 1, abort_flag, p.status)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t* trw = reinterpret_cast<const uint32_t*>(stage_t(st, dmat, dkt));
-                uint8_t* bt = stage_b(sb, dmat) + nt0 * 2 * kAtom;
-#pragma unroll kDecUnroll
-                for (int j = 0; j < ntn; ++j) {
-                    const uint32_t* tw = trw + (nt0 + j) * TileFmt<K>::words;
-                    uint32_t b[4];
-                    decode_tile<K>(tw, lw, k16, b);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) *reinterpret_cast<uint32_t*>(bt + j * 2 * kAtom + boff[q]) = b[q];
-                }
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    if (rank == 0)
-                        mbar_arrive(&full[sb]);
-                    else
-                        mbar_arrive_remote(mapa_rank(&full[sb], 0));
-                    mbar_arrive(&t_empty[st]);
-                }
-            }
-            if (!ok) break;
-            if (d >= kEpiWarps) continue;   // decode-only warp: on to the next unit's chunks
-            // ------------------------------- epilogue -------------------------------
-            if (!mbar_wait_bounded(acc_full, units_done & 1, abort_flag, p.status)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-            const int f0 = fb * kPairN;   // the unit's 128 features: TMEM column j is feature f0 + j
-#pragma unroll 1
-            for (int ei = 0; ei < Cfg::pmt / 2; ++ei) {
-                // this warp: pair M tile pm, rows pm*256 + 128*rank + 32*quarter + lane
-                const int pm = half * (Cfg::pmt / 2) + ei;
-                const int rbase = pm * kPairM + (int)rank * kBM + quarter * 32;
-                const int row = rbase + lane;
-                if (rbase >= rows) continue;   // warp-uniform: no row of this warp exists
-                float v[128];
-                if (MODE == 0) {
-                    const __half* svg = p.svh_a + (size_t)e * 2 * p.N + f0;
-                    gateup_epilogue(v, lane_addr + (uint32_t)(pm * 2 * kPairN), lane_addr + (uint32_t)((pm * 2 + 1) * kPairN),
-                                    svg, svg + p.N, p.suh_d + (size_t)e * p.N + f0, p.limit);
-                } else {
-                    tmem_ld128(lane_addr + (uint32_t)(pm * kPairN), v);
-                    out_block128(v, p.svh_a + (size_t)e * p.N + f0);
-                }
-                if (row < rows) {
-                    uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(row0 + row) * p.N + f0);
-#pragma unroll
-                    for (int c8 = 0; c8 < 16; ++c8) {
-                        uint4 o;
-                        o.x = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 0], v[c8 * 8 + 1]));
-                        o.y = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 2], v[c8 * 8 + 3]));
-                        o.z = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 4], v[c8 * 8 + 5]));
-                        o.w = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 6], v[c8 * 8 + 7]));
-                        dst[c8] = o;
-                    }
-                }
-            }
-            tc_fence_before();
-        }
-    }
-    __syncthreads();
-    cluster_sync_all();   // neither CTA leaves while the other (or the pair MMAs) may still touch it
-    if (warp == kWarpMma) {
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
     }
 }
 
@@ -1071,39 +653,6 @@ static cudaError_t make_map(CUtensorMap* m, const void* base, int rows, int K)
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// clusters of 2 CTAs (one per SM); as many pairs as can be resident at once, at most one per unit
-template <int MODE, int K>
-static cudaError_t launch_pair(const GemmParams& p, int units_bound, cudaStream_t st)
-{
-    using Cfg = PairCfg<MODE, K>;
-    const void* fn = (const void*)exl3_gemm_pair_kernel<MODE, K>;
-    cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::smem_bytes);
-    if (err != cudaSuccess) return err;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cudaLaunchConfig_t cfg = {};
-    cfg.blockDim = dim3(kGemmThreads, 1, 1);
-    cfg.dynamicSmemBytes = Cfg::smem_bytes;
-    cfg.stream = st;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    static int max_pairs = 0;   // per kernel instance; the same on every B200
-    if (max_pairs == 0) {
-        cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
-        int n = 0;
-        if ((err = cudaOccupancyMaxActiveClusters(&n, fn, &cfg)) != cudaSuccess) return err;
-        if (n < 1) return cudaErrorInvalidConfiguration;
-        max_pairs = n;
-    }
-    int pairs = units_bound < max_pairs ? units_bound : max_pairs;
-    if (pairs < 1) pairs = 1;
-    cfg.gridDim = dim3(2 * pairs, 1, 1);
-    return cudaLaunchKernelEx(&cfg, exl3_gemm_pair_kernel<MODE, K>, p);
-}
-
 template <int MODE, int K>
 static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
 {
@@ -1115,8 +664,7 @@ static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
     int* counters = reinterpret_cast<int*>(a.scratch);
     cudaError_t err;
     if (MODE == 0) {
-        const int rp0 = DSV41_GEMM_PAIR ? PairCfg<0, K>::rows_per_pass : GemmCfg<0, K>::rows_per_pass;
-        const int rp1 = DSV41_GEMM_PAIR ? PairCfg<1, K>::rows_per_pass : GemmCfg<1, K>::rows_per_pass;
+        const int rp0 = GemmCfg<0, K>::rows_per_pass, rp1 = GemmCfg<1, K>::rows_per_pass;
         gemm_plan_kernel<<<1, 32, 0, st>>>(a.fat_experts, a.n_fat, a.counts, a.offsets, rp0, rp1, passes0, counters, passes1,
                                            counters + 1);
         if ((err = cudaGetLastError()) != cudaSuccess) return err;
@@ -1150,8 +698,6 @@ static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
     p.status = a.status;
     p.limit = a.limit;
     p.k16 = 65536u;
-    if (DSV41_GEMM_PAIR)
-        return launch_pair<MODE, K>(p, max_passes(N, E, PairCfg<MODE, K>::rows_per_pass) * (p.N / kPairN), st);
     const size_t smem = Cfg::smem_bytes;
     if ((err = cudaFuncSetAttribute((const void*)exl3_gemm_kernel<MODE, K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)smem)) != cudaSuccess)
