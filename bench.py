@@ -168,8 +168,9 @@ def launches_per_step(T, fat):
     from dsv41_flash_offload_b200 import _lib  # noqa: F401
     N = T * TOPK
     perm = 1 if N <= 8192 else 3
-    # permute, prep, 2 decode-GEMV passes, combine (+ GEMM plan and 2 tcgen05 GEMM passes)
-    return perm + 1 + 2 + 1 + (3 if fat >= 0 else 0)
+    # permute, prep, 2 decode-GEMV passes, combine (+ GEMM plan and 2 tcgen05 GEMM passes when some expert
+    # can exceed the busy threshold: the library skips them when T * topk <= fat)
+    return perm + 1 + 2 + 1 + (3 if fat >= 0 and N > fat else 0)
 
 
 def time_steps(fn, K, W, dist_on):

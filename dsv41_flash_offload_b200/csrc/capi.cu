@@ -77,9 +77,12 @@ static int auto_split(int N, int E, int H, int I, int requested)
     const int r = gemv_stage_rows();
     auto fits = [&](int s) { return s >= 1 && (H / 16) % (s * r) == 0 && (I / 16) % (s * r) == 0; };
     if (requested > 0) return fits(requested) ? requested : 1;
+    // split K only while the gate/up units cannot occupy half the SMs: the partial sums and the fixed-order
+    // reduction cost more than they gain beyond that (measured on B200, T=1 top-8, 128 units: 108.8 us
+    // unsplit, 110.7 split 2, 120.0 split 4, 151 split 8; a lone expert group still splits 8 ways)
     const int groups = N < E ? (N > 0 ? N : 1) : E;
     const long long units = (long long)groups * (I / 128);
-    const long long target = 2LL * num_sms();
+    const long long target = num_sms() / 2;
     int s = 1;
     while (units * s < target && s < 8 && fits(s * 2)) s *= 2;
     return s;
@@ -272,6 +275,9 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
                                      cudaStream_t st)
 {
     const int H = layer->hidden, I = layer->intermediate;
+    // an expert takes the GEMM path with more than `fat` rows; no expert has more rows than the call's
+    // row bound, so small calls (e.g. decode with T * topk <= fat) launch no GEMM kernels at all
+    const bool gemm_on = fat >= 0 && rows_bound > fat;
     cudaError_t err;
     if (split > 1) {
         const size_t n = (size_t)(gemv_units_alloc(groups_bound, H, I, split) / split + 1) * 4;
@@ -312,7 +318,7 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
     gp.N = I;
     if ((err = launch_gemv(0, gp, gemv_units_bound(groups_bound, H, I, 0, split), st)) != cudaSuccess) return err;
     timer_mark(st, 3);
-    if (fat >= 0 && (err = launch_gemm_gateup(ga, st)) != cudaSuccess) return err;
+    if (gemm_on && (err = launch_gemm_gateup(ga, st)) != cudaSuccess) return err;
     timer_mark(st, 4);
     gp.tab_a = layer->down_ptrs;
     gp.tab_b = nullptr;
@@ -325,7 +331,7 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
     gp.N = H;
     if ((err = launch_gemv(1, gp, gemv_units_bound(groups_bound, I, H, 1, split), st)) != cudaSuccess) return err;
     timer_mark(st, 5);
-    if (fat >= 0 && (err = launch_gemm_down(ga, st)) != cudaSuccess) return err;
+    if (gemm_on && (err = launch_gemm_down(ga, st)) != cudaSuccess) return err;
     timer_mark(st, 6);
     return cudaSuccess;
 }
