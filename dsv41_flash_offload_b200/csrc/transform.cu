@@ -75,11 +75,12 @@ __device__ __forceinline__ void had128_quad(float (&v)[32], int hl)
             }
 #pragma unroll
     for (int m = 1; m < 4; m <<= 1) {
-        const bool upper = (hl & m) != 0;
+        // lower element: v + partner; upper: partner - v -- one FFMA with +-1 rounds exactly as the add
+        const float sg = (hl & m) ? -1.0f : 1.0f;
 #pragma unroll
         for (int q = 0; q < 32; ++q) {
             const float pv = __shfl_xor_sync(0xffffffffu, v[q], m);
-            v[q] = upper ? (pv - v[q]) : (v[q] + pv);
+            v[q] = fmaf(sg, v[q], pv);
         }
     }
 }
@@ -112,16 +113,23 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ XRows
             const int blk = 8 * j + g;
             const bool act = blk < nb;   // lanes past the last block transform a copy of block 0, unstored
             const int c = (act ? blk : 0) * 128 + hl * 32;
+            float xv[32];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float x8[8];
+                load8_as_half(xb, x_dtype, row * H + c + 8 * k, x8);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) xv[8 * k + q] = x8[q];
+            }
 #pragma unroll
             for (int m = 0; m < 2; ++m) {
                 float v[32];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    float xv[8], sv[8];
-                    load8_as_half(xb, x_dtype, row * H + c + 8 * k, xv);
+                    float sv[8];
                     load8_half(sg + (size_t)m * H + c + 8 * k, sv);
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) v[8 * k + q] = __fmul_rn(xv[q], sv[q]);
+                    for (int q = 0; q < 8; ++q) v[8 * k + q] = __fmul_rn(xv[8 * k + q], sv[q]);
                 }
                 had128_quad(v, hl);
                 __half* o = (m ? xt_u : xt_g) + (size_t)p * H + c;
