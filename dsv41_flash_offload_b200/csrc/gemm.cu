@@ -554,6 +554,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
             }
             if (!ok) break;
             // ------------------------------- epilogue -------------------------------
+            // the unit's scale rows (128 fp16 each) into L1 while the last MMAs finish
+            if (lane < 2 * (MODE == 0 ? 3 : 1)) {
+                const int which = lane >> 1;
+                const __half* sv = MODE == 0 ? (which == 2 ? p.suh_d + (size_t)e * p.N : p.svh_a + ((size_t)e * 2 + which) * p.N)
+                                             : p.svh_a + (size_t)e * p.N;
+                asm volatile("prefetch.global.L1 [%0];" ::"l"(sv + fb * kBN + (lane & 1) * 64));
+            }
             if (!mbar_wait_bounded(acc_full, units_done & 1, abort_flag, p.status)) {
                 ok = false;
                 break;
