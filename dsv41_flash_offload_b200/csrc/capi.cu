@@ -215,6 +215,16 @@ constexpr int kExpertGemmFat = 32;
 
 static int layer_bits(const dsv41_moe_layer* layer) { return layer->bits ? layer->bits : 3; }
 
+// the kernels move rows with 16- and 32-byte vector accesses and carve the workspace at 256-byte offsets
+static bool aligned_to(const void* p, size_t a) { return reinterpret_cast<uintptr_t>(p) % a == 0; }
+static int check_alignment(const void* x, const void* out, const void* workspace)
+{
+    if (x && !aligned_to(x, 16)) return fail(DSV41_E_INVALID, "activations must be 16-byte aligned");
+    if (out && !aligned_to(out, 16)) return fail(DSV41_E_INVALID, "out must be 16-byte aligned");
+    if (workspace && !aligned_to(workspace, 256)) return fail(DSV41_E_INVALID, "workspace must be 256-byte aligned");
+    return DSV41_OK;
+}
+
 static int check_layer(const dsv41_moe_layer* layer)
 {
     if (!layer) return fail(DSV41_E_INVALID, "layer is NULL");
@@ -380,6 +390,7 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     if (x_dtype < DSV41_DTYPE_F16 || x_dtype > DSV41_DTYPE_F32) return fail(DSV41_E_INVALID, "bad x_dtype %d", x_dtype);
     if (T > 0 && (!x || !ids || !weights || !out)) return fail(DSV41_E_INVALID, "NULL input/output pointer");
     if (!workspace) return fail(DSV41_E_INVALID, "workspace is NULL");
+    if ((rc = check_alignment(x, out, workspace))) return rc;
     const int E = layer->num_experts, H = layer->hidden, I = layer->intermediate;
     const dsv41_moe_options dflt{-1, 0.0f, nullptr, 0, 0, 0};
     const dsv41_moe_options& o = opt ? *opt : dflt;
@@ -496,6 +507,7 @@ int dsv41_ep_peer_forward(const dsv41_moe_layer* local_layer, const dsv41_ep_pee
     if (T < 0 || T > tcap || k <= 0) return fail(DSV41_E_INVALID, "T=%d (tokens_cap %d), topk=%d", T, tcap, k);
     if (x_dtype < DSV41_DTYPE_F16 || x_dtype > DSV41_DTYPE_F32) return fail(DSV41_E_INVALID, "bad x_dtype %d", x_dtype);
     if (T > 0 && (!x || !ids || !weights || !out)) return fail(DSV41_E_INVALID, "NULL input/output pointer");
+    if ((rc = check_alignment(x, out, nullptr))) return rc;
     const int tl = world * tcap;
     const int fat = (fat_threshold >= 0 && tl > fat_threshold) ? fat_threshold : -1;
     const PeerLayout P = make_peer_layout(world, tcap, k, e_loc, H, I, fat);
@@ -619,6 +631,7 @@ int dsv41_moe_forward_logits(const dsv41_moe_layer* layer, const void* x, int32_
     if (rc) return rc;
     if ((rc = check_router(r, layer->num_experts, topk))) return rc;
     if (!workspace) return fail(DSV41_E_INVALID, "workspace is NULL");
+    if ((rc = check_alignment(x, out, workspace))) return rc;
     const dsv41_moe_options dflt{-1, 0.0f, nullptr, 0, 0, 0};
     const dsv41_moe_options& o = opt ? *opt : dflt;
     const int fat = (o.fat_threshold >= 0 && T > o.fat_threshold) ? o.fat_threshold : -1;
@@ -653,6 +666,7 @@ int dsv41_permute(const int64_t* ids, const float* weights, int32_t T, int32_t t
     if (expert_map && map_len <= 0) return fail(DSV41_E_INVALID, "expert_map given with map_len %d", map_len);
     if (!workspace || workspace_bytes < dsv41_permute_workspace_size(T, topk, num_experts))
         return fail(DSV41_E_WORKSPACE, "permute workspace too small");
+    if (int rc = check_alignment(nullptr, nullptr, workspace)) return rc;
     const int N = T * topk;
     const size_t E1 = (size_t)num_experts + 1, n = (size_t)(N > 0 ? N : 1);
     size_t o = 0;
@@ -691,6 +705,7 @@ int dsv41_combine(const void* y, const int32_t* route_pos, const float* weights,
     if (T < 0 || topk <= 0 || hidden <= 0 || hidden % 8) return fail(DSV41_E_INVALID, "bad sizes");
     if (T == 0) return DSV41_OK;
     if (!y || !route_pos || !weights || !out) return fail(DSV41_E_INVALID, "NULL pointer");
+    if (int rc = check_alignment(y, out, nullptr)) return rc;
     cudaError_t err = launch_combine(static_cast<const __half*>(y), route_pos, weights, T, topk, hidden, accumulate, out,
                                      static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(err, "combine");
@@ -768,6 +783,7 @@ int dsv41_expert_gemm(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     if (n_experts == 0 || total_rows == 0) return DSV41_OK;
     if (!x || !experts || !counts || !offsets || !token_sorted || !weight_sorted || !out || !workspace)
         return fail(DSV41_E_INVALID, "NULL pointer");
+    if ((rc = check_alignment(x, out, workspace))) return rc;
     const int H = layer->hidden, I = layer->intermediate, E = layer->num_experts;
     size_t offs[16];
     const size_t need = expert_gemm_layout(total_rows, n_experts, H, I, offs);

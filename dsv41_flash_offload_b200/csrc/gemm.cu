@@ -193,6 +193,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, in
         : "memory");
 }
 
+// one 32-byte store (256-bit st.global on sm_100; `p` 32-byte aligned), not allocated in L1
+__device__ __forceinline__ void st_global_32B(void* p, const uint32_t (&o)[8])
+{
+    asm volatile("st.global.L1::no_allocate.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(o[0]),
+                 "r"(o[1]), "r"(o[2]), "r"(o[3]), "r"(o[4]), "r"(o[5]), "r"(o[6]), "r"(o[7])
+                 : "memory");
+}
+
 __device__ __forceinline__ void load_half8(const __half* p, float* dst)
 {
     const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
@@ -583,15 +591,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                     out_block128(v, p.svh_a + (size_t)e * p.N + fb * kBN);
                 }
                 if (row < rows) {
-                    uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)(row0 + row) * p.N + fb * kBN);
+                    // 256 B of the row as eight 32-byte stores (rows are 4-8 KB, blocks 256 B: 32-byte aligned)
+                    __half* dst = p.out + (size_t)(row0 + row) * p.N + fb * kBN;
 #pragma unroll
-                    for (int c8 = 0; c8 < 16; ++c8) {
-                        uint4 o;
-                        o.x = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 0], v[c8 * 8 + 1]));
-                        o.y = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 2], v[c8 * 8 + 3]));
-                        o.z = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 4], v[c8 * 8 + 5]));
-                        o.w = half2_as_u32(__floats2half2_rn(v[c8 * 8 + 6], v[c8 * 8 + 7]));
-                        dst[c8] = o;
+                    for (int c16 = 0; c16 < 8; ++c16) {
+                        uint32_t o[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            o[j] = half2_as_u32(__floats2half2_rn(v[c16 * 16 + 2 * j], v[c16 * 16 + 2 * j + 1]));
+                        st_global_32B(dst + c16 * 16, o);
                     }
                 }
             }

@@ -98,7 +98,8 @@ int dsv41_moe_workspace_size(int32_t T, int32_t topk, int32_t num_experts, int32
 
 /* out[T][H] (fp32, overwritten) = sum over valid routes (t, j) of weights[t][j] * expert(x[t]).
  *   x [T][H] of x_dtype (cast to fp16 first, as the reference does), ids [T][topk] int64
- *   (negative or >= E = skipped), weights [T][topk] fp32. */
+ *   (negative or >= E = skipped), weights [T][topk] fp32. x and out must be 16-byte aligned and
+ *   the workspace 256-byte aligned (DSV41_E_INVALID otherwise; device allocations are). */
 int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
                       const int64_t* ids, const float* weights, int32_t topk,
                       const dsv41_moe_options* opt, float* out, void* workspace,

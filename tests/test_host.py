@@ -137,6 +137,25 @@ def test_capi_rejects_bad_arguments_without_gpu():
     assert rc == _lib.E_INVALID
 
 
+def test_capi_rejects_misaligned_buffers_without_gpu():
+    # the pointers are never dereferenced: the argument checks run before any device work
+    L = _lib.load()
+    fake = 1 << 20
+    layer = _lib.MoeLayer(384, 4096, 2048, 0, *([fake] * 7))
+    ids = (C.c_int64 * 8)()
+    w = (C.c_float * 8)()
+
+    def fwd(x, out, ws):
+        return L.dsv41_moe_forward(C.byref(layer), C.c_void_p(x), 0, 1, ids, w, 8, None, C.c_void_p(out),
+                                   C.c_void_p(ws), 1 << 30, None)
+
+    assert fwd(fake + 8, fake, fake) == _lib.E_INVALID and b"16-byte aligned" in L.dsv41_last_error()
+    assert fwd(fake, fake + 4, fake) == _lib.E_INVALID and b"out must be 16-byte" in L.dsv41_last_error()
+    assert fwd(fake, fake, fake + 16) == _lib.E_INVALID and b"256-byte aligned" in L.dsv41_last_error()
+    rc = L.dsv41_combine(C.c_void_p(fake + 2), C.c_void_p(fake), C.c_void_p(fake), 1, 8, 4096, 0, C.c_void_p(fake), None)
+    assert rc == _lib.E_INVALID and b"16-byte aligned" in L.dsv41_last_error()
+
+
 def test_capi_workspace_sizes_grow_with_tokens():
     L = _lib.load()
     sizes = []
