@@ -7,8 +7,8 @@
 //                     out_block, SwiGLU clamp, fp16, down-input transform -> xt_d
 //   pass 1 (down):    D [rows x 128 features] = xt_d . W_d; epilogue: out_block -> y (fp16)
 // Work unit = (busy expert, row pass of 256 (gate/up) or 512 (down) rows, 128-feature block).
-// One CTA per SM, 12 warps, three independent mbarrier rings (activations, decoded weights,
-// trellis words):
+// One CTA per SM, 12 warps, two mbarrier rings (activations + decoded weights advance together under
+// one full/empty pair; trellis words run ahead in their own ring):
 //   warp 0     activation producer: TMA (cp.async.bulk.tensor, SWIZZLE_128B, into this CTA only) of
 //              128-row x 64-k tiles; a stage is reused once the MMAs that read it have committed
 //   warps 1, 3 TMEM allocator (warp 1, 512 columns) and two single-thread tcgen05.mma issuers
@@ -19,7 +19,8 @@
 //   warps 4-11 decoders: each lane decodes its 8 weights of a 16x16 tile in registers (the same
 //              exact decode as the GEMV) and stores them as K-major 128B-swizzled fp16 B-operand
 //              rows; after the last k chunk they are the epilogue (tcgen05.ld, one row per thread,
-//              128-point Hadamard in registers, intermediate results parked in TMEM)
+//              128-point Hadamard in registers, intermediate results parked in TMEM, the unit's scale
+//              rows prefetched into L1 while the last MMAs run, 32-byte row stores)
 // Experts with more rows than one pass reuse each decoded weight for 256/512 rows.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -76,9 +77,10 @@ constexpr int kTileB = kBN * kRowB;     // one 128-feature decoded weight tile
 template <int K>
 __host__ __device__ constexpr int tr_row() { return 8 * TileFmt<K>::bytes; }   // 8 n-tiles of one k-tile row (768 B at K = 3)
 
-// Three independent rings per CTA (each with full/empty mbarriers):
+// Rings per CTA (each with full/empty mbarriers):
 //   A (activations, TMA)   released by tcgen05.commit after the chunk's MMAs
-//   B (decoded weights)    written by the decoders, released by tcgen05.commit
+//   B (decoded weights)    written by the decoders, released by tcgen05.commit (with the merged ring,
+//                          A and B stages share one full barrier: TMA bytes + one arrival per decoder)
 //   T (trellis k-rows)     filled by the trellis producer, released by the decoders, so the
 //                          compressed words stream ahead of the MMAs by several chunks
 template <int MODE, int K>
