@@ -22,8 +22,13 @@ cpu_baseline / --impl reference = the reference's own AVX2 CPU expert tier
           (kernels/cpu_avx2/ft_tier_ext.cpp tier_forward, built into oracle/_ref) on the same
           decode batches, all host cores, rank 0 only.
 N > 1 (torchrun, one rank per GPU) runs the expert-parallel layer: each rank holds E/N experts and
-its own 64-token batch (weak scaling); fixed-slot NCCL all-to-all dispatch/combine, no host sync.
---workload ep40 / prefill-ep run BASELINE configs[3] / configs[4] instead (strong scaling).
+its own 64-token batch (weak scaling); the dispatch/combine exchange is done by peer loads inside the
+layer kernels (--ep peer, default) or by fixed-slot NCCL all-to-all (--ep nccl), no host sync. The same
+line then carries `ep_parity` (the first batch through the peer and NCCL paths vs the single-GPU
+layer of all experts on every rank; the run exits 3 if either is outside the parity bar), and `ep40` /
+`prefill_ep`: BASELINE configs[3] (40-layer stack, 256-token decode batch) and configs[4] (131,072
+tokens x 8 layers, Zipf(1.5)) measured in the same process (strong scaling; --no-stack skips them).
+--workload ep40 / prefill-ep run configs[3] / configs[4] alone as the line.
 """
 from __future__ import annotations
 
@@ -76,6 +81,8 @@ def parse():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-stack", action="store_true",
+                    help="N > 1: skip the configs[3] / configs[4] stack measurements that follow the decode line")
     ap.add_argument("--workload", choices=["decode", "prefill", "ep40", "prefill-ep"], default="decode",
                     help="decode: BASELINE configs[1] (default); prefill: configs[2] alone (one 16k-token Zipf(1.1) "
                          "batch, GEMM tensor roofline); ep40: configs[3] 40-layer stack, 256-token decode batch; "
@@ -294,23 +301,45 @@ def reference_cpu_tier(layer, batches, seconds, T):
                        cpu(layer.w13_svh[:, 1]), cpu(layer.w2_suh), cpu(layer.w2_svh))
     host = [(torch.from_numpy(x.astype(np.float16).astype(np.float32)), torch.from_numpy(ids.astype(np.int32)),
              torch.from_numpy(w)) for x, ids, w in batches]
-    mod.tier_forward(0, *host[0], -1)  # warm-up (page-in)
-    calls, t0 = 0, time.perf_counter()
-    per = []
-    while True:
-        x, sel, w = host[calls % len(host)]
-        t1 = time.perf_counter()
-        mod.tier_forward(0, x, sel, w, -1)
-        per.append(time.perf_counter() - t1)
-        calls += 1
-        if time.perf_counter() - t0 >= seconds and calls >= 3:
-            break
-    total = time.perf_counter() - t0
+    def timed(mode, secs):
+        mod.tier_forward(0, *host[0], mode)  # warm-up (page-in)
+        calls, t0 = 0, time.perf_counter()
+        per = []
+        while True:
+            x, sel, w = host[calls % len(host)]
+            t1 = time.perf_counter()
+            mod.tier_forward(0, x, sel, w, mode)
+            per.append(time.perf_counter() - t1)
+            calls += 1
+            if time.perf_counter() - t0 >= secs and calls >= 3:
+                break
+        return calls, time.perf_counter() - t0, statistics.median(per)
+
+    calls, total, med = timed(-1, seconds)
+    # EXACT mode (per-weight fp16 decode, the mode the GPU kernels match), a shorter sample
+    e_calls, e_total, e_med = timed(1, max(2.0, seconds / 3))
     mod.tier_stop()
+    build = f"{os.path.basename(os.path.dirname(path))} build of kernels/cpu_avx2/ft_tier_ext.cpp"
     return {"value": round(T * calls / total, 2), "unit": "tok/s", "cores": ncpu, "kind": "reference",
+            "cpu_model": cpu_model(),
             "sample": f"{calls} tier_forward calls (decode batches of {T} tokens x top-{TOPK}, mode -1 auto, "
-                      f"clamp {LIMIT}) in {total:.1f} s; median {statistics.median(per) * 1e3:.1f} ms/call; "
-                      f"{os.path.basename(os.path.dirname(path))} build of kernels/cpu_avx2/ft_tier_ext.cpp"}
+                      f"clamp {LIMIT}) in {total:.1f} s; median {med * 1e3:.1f} ms/call; {build}",
+            "exact_mode": {"value": round(T * e_calls / e_total, 2), "unit": "tok/s", "mode": 1,
+                           "sample": f"{e_calls} tier_forward calls, mode 1 (EXACT), in {e_total:.1f} s; "
+                                     f"median {e_med * 1e3:.1f} ms/call"}}
+
+
+def cpu_model():
+    """The host CPU's model name (first 'model name' line of /proc/cpuinfo) and its logical CPU count."""
+    name = "unknown"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                name = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return f"{name} ({os.cpu_count()} logical CPUs)"
 
 
 def prefill_measure(layers, dev, Tp, fat, tf_burst, tf_sus, peak_src, dist_on, n=6, num_experts=E, warm=3):
@@ -357,12 +386,7 @@ def run_prefill_workload(a, world, rank, dev, dist_on, tf_burst, tf_sus, peak_sr
     from dsv41_flash_offload_b200 import exl3
     layers = [exl3.Exl3MoELayer.synthetic(a.experts, H, I, seed=0, layer=l, device=dev) for l in range(a.layers)]
     fat = exl3.FAT_EXPERT_THRESHOLD
-    uuid = None
-    try:
-        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid).replace("GPU-", "")
-    except Exception:
-        pass
-    sampler = ClockSampler(uuid or str(dev.index))
+    sampler = ClockSampler(gpu_uuid(dev) or str(dev.index))
     pf = prefill_measure(layers, dev, a.prefill_tokens, fat, tf_burst, tf_sus, peak_src, dist_on,
                          n=max(a.steps, 1), num_experts=a.experts, warm=max(a.warmup, 3))
     clocks = sampler.stop()
@@ -384,10 +408,32 @@ def run_prefill_workload(a, world, rank, dev, dist_on, tf_burst, tf_sus, peak_sr
 
 # ------------------------------------------------------------------------------------------
 def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst, peak_src):
+    """BASELINE configs[3] (ep40) or configs[4] (prefill-ep) as the run's own line (--workload)."""
+    import torch
+    uuid = gpu_uuid(dev)
+    sampler = ClockSampler(uuid or str(local))
+    line = stack_measure(a, kind, world, rank, dev, dist_on, hbm)
+    line["clocks"] = sampler.stop()
+    if rank == 0:
+        EMIT(line)
+    if dist_on:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def gpu_uuid(dev):
+    import torch
+    try:
+        return "GPU-" + str(torch.cuda.get_device_properties(dev).uuid).replace("GPU-", "")
+    except Exception:
+        return None
+
+
+def stack_measure(a, kind, world, rank, dev, dist_on, hbm):
     """BASELINE configs[3] (ep40) and configs[4] (prefill-ep): a stack of MoE layers, experts sharded
-    E/world per rank (expert parallel, NCCL all-to-all) -- world 1 runs the same stack on one GPU.
-    Total tokens are fixed (strong scaling) and split evenly over the ranks; the next layer's input
-    is the residual x + moe(x)."""
+    E/world per rank (expert parallel) -- world 1 runs the same stack on one GPU. Total tokens are fixed
+    (strong scaling) and split evenly over the ranks; the next layer's input is the residual
+    x + moe(x). Returns the measurement as a bench line (every rank takes the same collective steps)."""
     import numpy as np
     import torch
     from dsv41_flash_offload_b200 import exl3, synth
@@ -408,11 +454,12 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
             ep.slot_capacity = T  # decode batches: fixed-slot dispatch, no host synchronisation
     g = torch.Generator(device=dev).manual_seed(7000 + rank)
     x0 = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
-    routes = []
-    for l in range(n_layers):
-        ids, w = synth.routing_np(9000 + 100 * rank + l, T, E, TOPK, kind="zipf" if zipf else "uniform",
-                                  zipf_s=zipf or 1.1)
-        routes.append((torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev)))
+
+    def route_np(r, l):
+        return synth.routing_np(9000 + 100 * r + l, T, E, TOPK, kind="zipf" if zipf else "uniform", zipf_s=zipf or 1.1)
+
+    routes_np = [route_np(rank, l) for l in range(n_layers)]
+    routes = [(torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev)) for ids, w in routes_np]
 
     def step(i):
         x = x0
@@ -423,35 +470,38 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
         return x
 
     steps, warm = (max(1, min(a.steps, 10)) if kind == "ep40" else max(1, min(a.steps, 3))), 3
-    uuid = None
-    try:
-        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid).replace("GPU-", "")
-    except Exception:
-        pass
-    sampler = ClockSampler(uuid or str(local))
     ms = time_steps(step, steps, warm, dist_on)
-    clocks = sampler.stop()
     for e in eps:
         e.stats = {k: 0 for k in e.stats}
-    st = stage_times(step, 1, 0)  # one step, per-stage times summed over its layers' local forwards
-    local_ms = sum(st.values()) * n_layers   # stage_times averages over calls (n_layers per step)
+    st = stage_times(step, 1, 0)  # one step, per-stage times averaged over its layers' local forwards
+    local_ms = sum(st.values()) * n_layers
     if peer is not None:   # the exchange waits sit inside the permute and combine stages
         local_ms -= (st.get("permute", 0.0) + st.get("combine", 0.0)) * n_layers
     recv = sum(e.stats["recv_rows"] for e in eps)
     a2a = sum(e.stats["a2a_bytes_out"] + e.stats["a2a_bytes_back"] for e in eps)
+    # every rank's routing of every layer is regenerated here from its seed (no collective needed): the
+    # routes each rank serves and the gate/up decode-GEMV bytes of this rank's local forwards
+    if kind == "ep40":
+        all_ids = [[route_np(r, l)[0] for r in range(world)] for l in range(n_layers)]
+        gu = [gateup_bytes_ep(all_ids[l], lo, hi)[0] for l in range(n_layers)]
+        gemv_frac = statistics.mean(gu) / (st["gemv_gateup"] / 1e3) / 1e9 / hbm if st["gemv_gateup"] > 0 else None
+    else:
+        gemv_frac = None
     if peer is not None:
         # routes each rank serves (summed over all ranks' tokens and all layers) and the bytes this rank
         # pulls: token rows of the routes it serves + expert outputs of its own valid routes
-        dest = torch.zeros(world, dtype=torch.float64, device=dev)
+        dest = np.zeros(world)
         own = 0
-        for ids, _ in routes:
-            v = ids[(ids >= 0) & (ids < E)]
-            dest += torch.bincount(v // e_loc, minlength=world)[:world].double()
-            own += int(v.numel())
-        if dist_on:
-            torch.distributed.all_reduce(dest)
+        for l in range(n_layers):
+            for r in range(world):
+                v = all_ids[l][r].reshape(-1)
+                v = v[(v >= 0) & (v < E)]
+                dest += np.bincount(v // e_loc, minlength=world)[:world]
+                if r == rank:
+                    own += int(v.size)
         recv = float(dest[rank])
         a2a = (recv + own) * H * 2
+        peer.close()
     t = torch.tensor([recv, a2a, local_ms], dtype=torch.float64, device=dev)
     allv = [torch.zeros_like(t) for _ in range(world)]
     if dist_on:
@@ -474,7 +524,7 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
                                                   if peer is not None else "NCCL all-to-all dispatch/combine"))
                                       if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (every step streams the routed experts of all layers)"},
-            "layer_tok_s": round(value * n_layers, 1), "clocks": clocks,
+            "layer_tok_s": round(value * n_layers, 1),
             "ep": {"exchange": "peer memory" if peer is not None else "NCCL all-to-all",
                    ("routes_served_per_gpu_per_step" if peer is not None else "rows_per_gpu_per_step"):
                        [round(r, 1) for r in rows],
@@ -483,11 +533,12 @@ def run_stack_workload(a, kind, world, rank, local, dev, dist_on, hbm, tf_burst,
                        [round(float(v[1])) for v in allv],
                    "local_moe_ms_per_step": [round(float(v[2]), 3) for v in allv],
                    "a2a_and_dispatch_share": round(max(0.0, 1.0 - max(float(v[2]) for v in allv) / (ms / steps)), 4)}}
-    if rank == 0:
-        EMIT(line)
-    if dist_on:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
+    if gemv_frac is not None:
+        line["ep"]["gemv_gateup_hbm_frac_rank0_layers"] = round(gemv_frac, 4)
+    del layers, eps, routes
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return line
 
 
 def main():
@@ -569,11 +620,7 @@ def main():
         x, ids, w = batches[i % len(batches)]
         forward(i, x, ids, w, out)
 
-    uuid = None
-    try:
-        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid).replace("GPU-", "")
-    except Exception:
-        pass
+    uuid = gpu_uuid(dev)
     # clocks are sampled from the first timed step through the end-to-end timed steps (two timed
     # regions of K steps and the stage-timing pass between them): short steps at large N leave too
     # few 50 ms samples inside one region alone
@@ -681,6 +728,24 @@ def main():
                       "step_ms": round(ms / a.steps, 5),
                       "a2a_and_dispatch_share": round(max(0.0, 1.0 - local_ms / (ms / a.steps)), 4)}
 
+    parity_ok = True
+    if world > 1:
+        line["ep_parity"] = ep_parity_check(peer, layers, batches, dev, world, T)
+        parity_ok = line["ep_parity"]["ok"]
+        if peer is not None:
+            peer.close()
+        if not a.no_stack:
+            # BASELINE configs[3] and configs[4] in the same run (strong scaling); the decode layers go first
+            del layers, eps, peer, forward, step, e2e_step
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+            for key, kind in (("ep40", "ep40"), ("prefill_ep", "prefill-ep")):
+                sl = stack_measure(a, kind, world, rank, dev, dist_on, hbm)
+                line[key] = {"workload": sl["config"]["workload"], "parallelism": sl["config"]["parallelism"],
+                             "tok_s": sl["value"], "ms_per_step": sl["ms_per_step"], "steps": sl["steps"],
+                             "warmup": sl["warmup"], "scaling": "strong", "layer_tok_s": sl["layer_tok_s"],
+                             "ep": sl["ep"]}
+
     if not a.no_sweep and world == 1:
         sweep = {}
         for Ts in (1, 8, 32, 64):
@@ -716,6 +781,43 @@ def main():
     if dist_on:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+    if not parity_ok:
+        sys.stderr.write(f"expert-parallel output outside the parity bar: {line.get('ep_parity')}\n")
+        sys.exit(3)
+
+
+def ep_parity_check(peer, layers, batches, dev, world, T):
+    """Expert-parallel output of this run's first routing batch (layer 0) through the peer-memory path
+    (when it is the one timed) and through the NCCL fixed-slot path, against the single-GPU layer of all
+    E experts -- the layer the GPU tests pin to the oracle -- on every rank. Max-abs and cosine are
+    reduced over the ranks (max / min). Bar: max-abs 2e-2, cosine 0.9999."""
+    import torch
+    from dsv41_flash_offload_b200 import exl3
+    from dsv41_flash_offload_b200.ep import EPMoE, local_layer_fn
+    full = exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, layer=0, device=dev)
+    x, ids, w = batches[0]
+    ref = exl3.apply_exl3_fused_moe(x, ids, w, full, None, None, LIMIT)
+    nccl = EPMoE(local_layer_fn(layers[0], LIMIT), E)
+    nccl.slot_capacity = T
+    outs = {"nccl_fixed_slots": nccl(x, ids, w)}
+    if peer is not None:
+        outs["peer_memory"] = peer(x, ids, w, layer=layers[0])
+    res = {}
+    for name, out in sorted(outs.items()):
+        d = (out - ref).abs().max().double()
+        r, o = ref.double().reshape(-1), out.double().reshape(-1)
+        cos = (r @ o) / torch.sqrt(torch.clamp((r @ r) * (o @ o), min=1e-300))
+        v = torch.stack([d, -cos]).reshape(2)
+        torch.distributed.all_reduce(v, op=torch.distributed.ReduceOp.MAX)
+        res[name] = {"max_abs": float(v[0]), "cos": round(-float(v[1]), 8)}
+    st = torch.tensor([exl3.read_status(device=dev) + (peer.read_status() if peer is not None else 0)],
+                      device=dev)
+    torch.distributed.all_reduce(st, op=torch.distributed.ReduceOp.MAX)
+    ok = all(r["max_abs"] <= 2e-2 and r["cos"] >= 0.9999 for r in res.values()) and int(st.item()) == 0
+    del full, ref, outs
+    torch.cuda.empty_cache()
+    return {**res, "tokens": world * T, "reference": "single-GPU layer of all 384 experts (oracle-pinned)",
+            "tolerance": {"max_abs": 2e-2, "cos": 0.9999}, "status": int(st.item()), "ok": ok}
 
 
 if __name__ == "__main__":

@@ -18,13 +18,16 @@ OK, E_INVALID, E_CUDA, E_WORKSPACE = 0, -1, -2, -3
 # exported symbols, in include/dsv41_b200.h order
 SYMBOLS = (
     "dsv41_last_error", "dsv41_abi_version", "dsv41_build_info", "dsv41_moe_workspace_size",
-    "dsv41_moe_forward", "dsv41_moe_forward_noalloc", "dsv41_permute_workspace_size", "dsv41_permute", "dsv41_combine",
-    "dsv41_decode_dense", "dsv41_decode_dense_bits", "dsv41_expert_gemm", "dsv41_expert_gemm_workspace_size", "dsv41_read_status", "dsv41_wait_selftest",
+    "dsv41_moe_forward", "dsv41_moe_forward_noalloc", "dsv41_moe_noalloc_read_status",
+    "dsv41_permute_workspace_size", "dsv41_permute", "dsv41_combine",
+    "dsv41_decode_dense", "dsv41_decode_dense_bits", "dsv41_expert_gemm", "dsv41_expert_gemm_workspace_size",
+    "dsv41_read_status", "dsv41_wait_selftest",
     "dsv41_router_topk", "dsv41_moe_forward_logits",
     "dsv41_ep_peer_buffer_size", "dsv41_ep_peer_alloc", "dsv41_ep_peer_open", "dsv41_ep_peer_close", "dsv41_ep_peer_free",
     "dsv41_ep_peer_forward", "dsv41_ep_peer_read_status",
     "dsv41_set_stage_timing", "dsv41_read_stage_times",
 )
+ABI_VERSION = 2
 MAX_PEERS = 8
 IPC_HANDLE_BYTES = 64
 N_STAGES = 7
@@ -50,7 +53,7 @@ class RouterOptions(C.Structure):
 
 class EpPeerGroup(C.Structure):
     _fields_ = [("rank", C.c_int32), ("world", C.c_int32), ("num_global_experts", C.c_int32),
-                ("tokens_cap", C.c_int32), ("bases", C.c_void_p * MAX_PEERS)]
+                ("tokens_cap", C.c_int32), ("bases", C.c_void_p * MAX_PEERS), ("wait_limit_us", C.c_int32)]
 
 
 class Dsv41Error(RuntimeError):
@@ -84,6 +87,8 @@ def load(path: str | None = None):
         L.dsv41_moe_forward_noalloc.restype = C.c_int
         L.dsv41_moe_forward_noalloc.argtypes = [C.POINTER(MoeLayer), vp, i32, i32, i64p, vp, i32, C.POINTER(MoeOptions),
                                                 vp, vp]
+        L.dsv41_moe_noalloc_read_status.restype = C.c_int
+        L.dsv41_moe_noalloc_read_status.argtypes = [vp, C.POINTER(C.c_int32)]
         L.dsv41_permute_workspace_size.restype = C.c_size_t
         L.dsv41_permute_workspace_size.argtypes = [i32, i32, i32]
         L.dsv41_permute.restype = C.c_int
@@ -129,7 +134,7 @@ def load(path: str | None = None):
         L.dsv41_set_stage_timing.argtypes = [i32]
         L.dsv41_read_stage_times.restype = C.c_int
         L.dsv41_read_stage_times.argtypes = [C.POINTER(C.c_float), i32, C.POINTER(C.c_int32)]
-        if L.dsv41_abi_version() != 1:
+        if L.dsv41_abi_version() != ABI_VERSION:
             raise Dsv41Error("libdsv41_b200.so ABI version mismatch")
         _lib = L
         return L

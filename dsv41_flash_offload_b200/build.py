@@ -2,8 +2,9 @@
 
     python -m dsv41_flash_offload_b200.build [--verbose]
 
-nvcc -gencode arch=compute_100a,code=sm_100a -lineinfo -O3; the CUDA runtime is linked
-statically so the library only needs the driver (and coexists with torch's own runtime).
+nvcc -gencode arch=compute_100a,code=sm_100a -lineinfo -O3, one object per source file (compiled in
+parallel under _build/), then one link; the CUDA runtime is linked statically so the library only
+needs the driver (and coexists with torch's own runtime).
 """
 from __future__ import annotations
 
@@ -45,22 +46,37 @@ def needs_build() -> bool:
 def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = False) -> str:
     if not force and not needs_build():
         return LIB
+    from concurrent.futures import ThreadPoolExecutor
+
     nvcc = nvcc_path()
     ver = nvcc_version(nvcc)
-    cmd = [nvcc, *ARCH, "-lineinfo", "-O3", "-std=c++17", "--use_fast_math=false", "-shared",
-           "-Xcompiler", "-fPIC", "-cudart", "static", f'-DDSV41_NVCC_VERSION="{ver}"',
-           "-o", LIB + ".tmp"] + [os.path.join(CSRC, s) for s in SOURCES]
-    cmd = [c for c in cmd if c != "--use_fast_math=false"]
+    flags = [*ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", f'-DDSV41_NVCC_VERSION="{ver}"']
     if ptxas_verbose:
-        cmd.insert(1, "-Xptxas=-v")
-    if verbose:
-        print(" ".join(cmd), flush=True)
-    r = subprocess.run(cmd, capture_output=True, text=True)
+        flags.insert(0, "-Xptxas=-v")
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+
+    def compile_one(src):
+        obj = os.path.join(objdir, src.replace(".cu", ".o"))
+        cmd = [nvcc, *flags, "-c", "-o", obj, os.path.join(CSRC, src)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        return obj, subprocess.run(cmd, capture_output=True, text=True)
+
+    # one nvcc per source file, in parallel, then one link step
+    with ThreadPoolExecutor(max_workers=min(len(SOURCES), os.cpu_count() or 1)) as ex:
+        results = list(ex.map(compile_one, SOURCES))
+    for _, r in results:
+        if r.returncode != 0:
+            sys.stderr.write(r.stdout + r.stderr)
+            raise RuntimeError("nvcc failed building libdsv41_b200.so")
+        if verbose or ptxas_verbose:
+            sys.stderr.write(r.stderr)
+    link = [nvcc, *ARCH, "-shared", "-cudart", "static", "-o", LIB + ".tmp"] + [o for o, _ in results]
+    r = subprocess.run(link, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)
-        raise RuntimeError("nvcc failed building libdsv41_b200.so")
-    if verbose or ptxas_verbose:
-        sys.stderr.write(r.stderr)
+        raise RuntimeError("nvcc failed linking libdsv41_b200.so")
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

@@ -206,7 +206,15 @@ static int check_group(const dsv41_ep_peer_group* g)
     if (g->tokens_cap <= 0) return fail(DSV41_E_INVALID, "tokens_cap %d", g->tokens_cap);
     for (int d = 0; d < g->world; ++d)
         if (!g->bases[d]) return fail(DSV41_E_INVALID, "base of rank %d is NULL", d);
+    if (g->wait_limit_us < 0 || g->wait_limit_us > 2000000)
+        return fail(DSV41_E_INVALID, "wait_limit_us %d out of range (0 = default, 1..2000000)", g->wait_limit_us);
     return DSV41_OK;
+}
+
+// limit of each wait for the peers' step stamps
+static uint64_t peer_wait_limit_ns(const dsv41_ep_peer_group* g)
+{
+    return g->wait_limit_us > 0 ? (uint64_t)g->wait_limit_us * 1000ull : kWaitLimitNs;
 }
 
 // run_batch semantics: listed experts with more rows than this use the tcgen05 GEMM, the rest the
@@ -237,6 +245,21 @@ static int check_layer(const dsv41_moe_layer* layer)
         return fail(DSV41_E_INVALID, "layer has a NULL tensor pointer");
     if (layer->bits != 0 && (layer->bits < 2 || layer->bits > 4))
         return fail(DSV41_E_INVALID, "bits %d per weight (2, 3 or 4)", layer->bits);
+    return DSV41_OK;
+}
+
+int validate_forward(const dsv41_moe_layer* layer, const void* x, int x_dtype, int T, const int64_t* ids,
+                     const float* weights, int topk, const dsv41_moe_options* opt, const float* out)
+{
+    int rc = check_layer(layer);
+    if (rc) return rc;
+    if (T < 0 || topk <= 0) return fail(DSV41_E_INVALID, "bad T=%d topk=%d", T, topk);
+    if (x_dtype < DSV41_DTYPE_F16 || x_dtype > DSV41_DTYPE_F32) return fail(DSV41_E_INVALID, "bad x_dtype %d", x_dtype);
+    if (T > 0 && (!x || !ids || !weights || !out)) return fail(DSV41_E_INVALID, "NULL input/output pointer");
+    if ((rc = check_alignment(x, out, nullptr))) return rc;
+    if (opt && opt->expert_map && opt->map_len <= 0)
+        return fail(DSV41_E_INVALID, "expert_map given with map_len %d", opt->map_len);
+    if (opt && opt->max_routes < 0) return fail(DSV41_E_INVALID, "max_routes %d < 0", opt->max_routes);
     return DSV41_OK;
 }
 
@@ -384,18 +407,13 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
                       const float* weights, int32_t topk, const dsv41_moe_options* opt, float* out, void* workspace,
                       size_t workspace_bytes, void* stream)
 {
-    int rc = check_layer(layer);
+    int rc = validate_forward(layer, x, x_dtype, T, ids, weights, topk, opt, out);
     if (rc) return rc;
-    if (T < 0 || topk <= 0) return fail(DSV41_E_INVALID, "bad T=%d topk=%d", T, topk);
-    if (x_dtype < DSV41_DTYPE_F16 || x_dtype > DSV41_DTYPE_F32) return fail(DSV41_E_INVALID, "bad x_dtype %d", x_dtype);
-    if (T > 0 && (!x || !ids || !weights || !out)) return fail(DSV41_E_INVALID, "NULL input/output pointer");
     if (!workspace) return fail(DSV41_E_INVALID, "workspace is NULL");
-    if ((rc = check_alignment(x, out, workspace))) return rc;
+    if ((rc = check_alignment(nullptr, nullptr, workspace))) return rc;
     const int E = layer->num_experts, H = layer->hidden, I = layer->intermediate;
     const dsv41_moe_options dflt{-1, 0.0f, nullptr, 0, 0, 0};
     const dsv41_moe_options& o = opt ? *opt : dflt;
-    if (o.expert_map && o.map_len <= 0) return fail(DSV41_E_INVALID, "expert_map given with map_len %d", o.map_len);
-    if (o.max_routes < 0) return fail(DSV41_E_INVALID, "max_routes %d < 0", o.max_routes);
     const int fat = (o.fat_threshold >= 0 && T > o.fat_threshold) ? o.fat_threshold : -1;  // fat_possible
     const Layout L = make_layout(T, topk, E, H, I, o.split_k, fat, o.max_routes);
     if (workspace_bytes < L.total)
@@ -533,7 +551,8 @@ int dsv41_ep_peer_forward(const dsv41_moe_layer* local_layer, const dsv41_ep_pee
     int64_t* ids_loc = reinterpret_cast<int64_t*>(own + P.ids_loc[p]);
     float* w_loc = reinterpret_cast<float*>(own + P.w_loc[p]);
     if ((err = launch_ep_gather(peers, world, rank, tcap, k, rank * e_loc, (rank + 1) * e_loc, stamp,
-                                P.ctrl + kCtrlInFlags, P.ids[p], P.w[p], ids_loc, w_loc, xstatus, st)) != cudaSuccess)
+                                P.ctrl + kCtrlInFlags, P.ids[p], P.w[p], ids_loc, w_loc, xstatus, peer_wait_limit_ns(g),
+                                st)) != cudaSuccess)
         return cuda_fail(err, "ep gather");
     // 3. the local forward over world * tcap tokens, token rows read from their ranks
     const PermBuffers pb = perm_buffers(ws, L);
@@ -560,7 +579,8 @@ int dsv41_ep_peer_forward(const dsv41_moe_layer* local_layer, const dsv41_ep_pee
     if (T > 0 &&
         (err = launch_ep_combine(peers, world, rank, tcap, k, e_loc, stamp, P.ctrl + kCtrlOutFlags,
                                  reinterpret_cast<const int*>(own + P.ids[p]), reinterpret_cast<const float*>(own + P.w[p]),
-                                 T, H, P.ws[p] + L.route_pos, P.ws[p] + L.y, out, xstatus, st)) != cudaSuccess)
+                                 T, H, P.ws[p] + L.route_pos, P.ws[p] + L.y, out, xstatus, peer_wait_limit_ns(g),
+                                 st)) != cudaSuccess)
         return cuda_fail(err, "ep combine");
     timer_end(st);
     return DSV41_OK;

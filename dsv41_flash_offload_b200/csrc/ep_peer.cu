@@ -19,8 +19,9 @@
 // Buffers alternate by step parity; a rank only publishes step s after it has seen every peer's
 // step s-1 stamp, which each peer writes only after finishing its step s-2 reads, so no buffer is
 // overwritten while a peer may still read it. Stamps are step + 1 (0 = nothing published).
-// All waits are bounded by %globaltimer: on expiry the kernel records status 1 in the control
-// block, writes an empty result and returns (no trap). Plain peer loads and stores only.
+// All waits are bounded by %globaltimer (the group's wait_limit_us, 2 s by default): on expiry the
+// kernel records status 1 in the control block, writes an empty result and returns (no trap). Plain
+// peer loads and stores only.
 #include "common.cuh"
 #include "internal.h"
 
@@ -38,9 +39,9 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v)
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// thread 0 of the block waits until every peer's stamp in flags[0..world) reached `stamp`;
-// returns false for the whole block on timeout (and records kStatusWaitTimeout)
-__device__ bool block_wait_stamps(const uint32_t* flags, int world, uint32_t stamp, int* status)
+// thread 0 of the block waits until every peer's stamp in flags[0..world) reached `stamp`, at most
+// limit_ns in all; returns false for the whole block on timeout (and records kStatusWaitTimeout)
+__device__ bool block_wait_stamps(const uint32_t* flags, int world, uint32_t stamp, int* status, uint64_t limit_ns)
 {
     __shared__ int ok;
     if (threadIdx.x == 0) {
@@ -49,7 +50,7 @@ __device__ bool block_wait_stamps(const uint32_t* flags, int world, uint32_t sta
         for (int d = 0; d < world && ok; ++d) {
             uint32_t it = 0;
             while ((int)(ld_acquire_sys(flags + d) - stamp) < 0) {
-                if ((++it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+                if ((++it & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) {
                     atomicExch(status, kStatusWaitTimeout);
                     ok = 0;
                     break;
@@ -98,11 +99,12 @@ __global__ void ep_signal_kernel(PeerTable peers, int world, int rank, size_t fl
 
 __global__ void __launch_bounds__(256) ep_gather_kernel(PeerTable peers, int world, int rank, int tcap, int k, int lo,
                                                         int hi, uint32_t stamp, size_t in_flags_off, size_t ids_off,
-                                                        size_t w_off, int64_t* ids_loc, float* w_loc, int* status)
+                                                        size_t w_off, int64_t* ids_loc, float* w_loc, int* status,
+                                                        uint64_t limit_ns)
 {
     const uint32_t* flags =
         reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(peers.base[rank]) + in_flags_off);
-    const bool ok = block_wait_stamps(flags, world, stamp, status);
+    const bool ok = block_wait_stamps(flags, world, stamp, status, limit_ns);
     const long long per = (long long)tcap * k, n = per * world;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         int64_t le = -1;
@@ -126,11 +128,12 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(PeerTable peers, int wor
 __global__ void __launch_bounds__(256) ep_combine_kernel(PeerTable peers, int world, int rank, int tcap, int k,
                                                          int e_loc, uint32_t stamp, size_t out_flags_off,
                                                          const int* ids, const float* w, int T, int H,
-                                                         size_t route_pos_off, size_t y_off, float* out, int* status)
+                                                         size_t route_pos_off, size_t y_off, float* out, int* status,
+                                                         uint64_t limit_ns)
 {
     const uint32_t* flags =
         reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(peers.base[rank]) + out_flags_off);
-    const bool ok = block_wait_stamps(flags, world, stamp, status);
+    const bool ok = block_wait_stamps(flags, world, stamp, status, limit_ns);
     const int chunks = H / 8;
     const long long n = (long long)T * chunks;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
@@ -187,19 +190,20 @@ cudaError_t launch_ep_signal(const PeerTable& peers, int world, int rank, size_t
 
 cudaError_t launch_ep_gather(const PeerTable& peers, int world, int rank, int tcap, int k, int lo, int hi,
                              uint32_t stamp, size_t in_flags_off, size_t ids_off, size_t w_off, int64_t* ids_loc,
-                             float* w_loc, int* status, cudaStream_t st)
+                             float* w_loc, int* status, uint64_t limit_ns, cudaStream_t st)
 {
     ep_gather_kernel<<<grid_for((long long)world * tcap * k, 256, 4), 256, 0, st>>>(
-        peers, world, rank, tcap, k, lo, hi, stamp, in_flags_off, ids_off, w_off, ids_loc, w_loc, status);
+        peers, world, rank, tcap, k, lo, hi, stamp, in_flags_off, ids_off, w_off, ids_loc, w_loc, status, limit_ns);
     return cudaGetLastError();
 }
 
 cudaError_t launch_ep_combine(const PeerTable& peers, int world, int rank, int tcap, int k, int e_loc, uint32_t stamp,
                               size_t out_flags_off, const int* ids, const float* w, int T, int H, size_t route_pos_off,
-                              size_t y_off, float* out, int* status, cudaStream_t st)
+                              size_t y_off, float* out, int* status, uint64_t limit_ns, cudaStream_t st)
 {
     ep_combine_kernel<<<grid_for((long long)T * (H / 8), 256, 16), 256, 0, st>>>(
-        peers, world, rank, tcap, k, e_loc, stamp, out_flags_off, ids, w, T, H, route_pos_off, y_off, out, status);
+        peers, world, rank, tcap, k, e_loc, stamp, out_flags_off, ids, w, T, H, route_pos_off, y_off, out, status,
+        limit_ns);
     return cudaGetLastError();
 }
 

@@ -182,21 +182,24 @@ __global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv
         for (int st = 0; st < stages_per_unit; ++st, ++it) {
             const int stage = it % kStages;
             const uint32_t round = it / kStages;
-            mbar_wait_bounded(&S.full[stage], round & 1, &S.abort_flag, p.status);
-            // this warp's tiles sit at byte offset tile * 32K of each staged 16-tile k-row
-            const uint32_t* trow = reinterpret_cast<const uint32_t*>(S.tr[stage]) + tile0 * kTW;
-            const uint32_t xaddr = smem_addr(S.x[stage][mat]) + x_lane;
+            // a wait that runs out (or a CTA that already gave up) skips the stage's compute: the
+            // staged bytes may never have arrived. The warp still takes every barrier step below.
+            if (mbar_wait_bounded(&S.full[stage], round & 1, &S.abort_flag, p.status)) {
+                // this warp's tiles sit at byte offset tile * 32K of each staged 16-tile k-row
+                const uint32_t* trow = reinterpret_cast<const uint32_t*>(S.tr[stage]) + tile0 * kTW;
+                const uint32_t xaddr = smem_addr(S.x[stage][mat]) + x_lane;
 #pragma unroll
-            for (int r = 0; r < kStageRows; ++r) {
-                uint32_t a[4];
-                ldmatrix_x4(a, xaddr + r * 32);
+                for (int r = 0; r < kStageRows; ++r) {
+                    uint32_t a[4];
+                    ldmatrix_x4(a, xaddr + r * 32);
 #pragma unroll
-                for (int t = 0; t < kTilesPerWarp; ++t) {
-                    const uint32_t* tw = trow + r * (kRowBytes / 4) + t * kTW;
-                    uint32_t b[4];
-                    decode_tile<K>(tw, lw, k16, b);
-                    mma_16816(acc[t][0], a, b[0], b[1]);
-                    mma_16816(acc[t][1], a, b[2], b[3]);
+                    for (int t = 0; t < kTilesPerWarp; ++t) {
+                        const uint32_t* tw = trow + r * (kRowBytes / 4) + t * kTW;
+                        uint32_t b[4];
+                        decode_tile<K>(tw, lw, k16, b);
+                        mma_16816(acc[t][0], a, b[0], b[1]);
+                        mma_16816(acc[t][1], a, b[2], b[3]);
+                    }
                 }
             }
             __syncwarp();
@@ -243,8 +246,16 @@ __global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv
             named_bar_sync(1, kConsumerWarps * 32);
         }
 
-        // epilogue: warp w transforms rows w, w + kConsumerWarps, ... of the group
+        // epilogue: warp w transforms rows w, w + kConsumerWarps, ... of the group. Once this CTA has
+        // given up on a wait, its remaining rows are written as zeros (the status word says why).
+        const bool aborted = *reinterpret_cast<volatile int*>(&S.abort_flag) != 0;
         for (int j = warp; j < rows; j += kConsumerWarps) {
+            if (aborted) {
+                const int n = MODE == 0 ? 128 : 256;
+                for (int c = lane * 4; c < n; c += 128)
+                    *reinterpret_cast<uint2*>(p.out + (size_t)(row0 + j) * p.N + cb * n + c) = make_uint2(0u, 0u);
+                continue;
+            }
             if (MODE == 0) {
                 float gv[4], uv[4];
 #pragma unroll

@@ -67,10 +67,10 @@ cudaError_t launch_ep_signal(const PeerTable& peers, int world, int rank, size_t
                              cudaStream_t st);
 cudaError_t launch_ep_gather(const PeerTable& peers, int world, int rank, int tcap, int k, int lo, int hi,
                              uint32_t stamp, size_t in_flags_off, size_t ids_off, size_t w_off, int64_t* ids_loc,
-                             float* w_loc, int* status, cudaStream_t st);
+                             float* w_loc, int* status, uint64_t limit_ns, cudaStream_t st);
 cudaError_t launch_ep_combine(const PeerTable& peers, int world, int rank, int tcap, int k, int e_loc, uint32_t stamp,
                               size_t out_flags_off, const int* ids, const float* w, int T, int H, size_t route_pos_off,
-                              size_t y_off, float* out, int* status, cudaStream_t st);
+                              size_t y_off, float* out, int* status, uint64_t limit_ns, cudaStream_t st);
 
 // Work lists for an explicit expert list over caller-permuted rows (run_batch semantics):
 // int32 counts/offsets copies, expert_sorted (-1 for rows of unlisted experts), GEMV groups of the
@@ -118,5 +118,17 @@ int num_sms();
 
 // record a message for dsv41_last_error() and return `code`
 int set_error(int code, const char* fmt, ...);
+
+}  // namespace dsv41
+
+struct dsv41_moe_layer;
+struct dsv41_moe_options;
+
+namespace dsv41 {
+
+// every argument check of dsv41_moe_forward except the workspace ones (size, NULL, alignment):
+// DSV41_OK or the error code, with the message recorded for dsv41_last_error()
+int validate_forward(const dsv41_moe_layer* layer, const void* x, int x_dtype, int T, const int64_t* ids,
+                     const float* weights, int topk, const dsv41_moe_options* opt, const float* out);
 
 }  // namespace dsv41

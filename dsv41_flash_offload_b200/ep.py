@@ -168,7 +168,9 @@ class EPPeerMoE:
     """
 
     def __init__(self, layer, num_global_experts: int, tokens_cap: int, topk: int, group=None,
-                 limit: float | None = 10.0, fat_threshold: int | None = None):
+                 limit: float | None = 10.0, fat_threshold: int | None = None, wait_limit_us: int = 0):
+        """wait_limit_us bounds each device-side wait for the peers' step stamps (0 = 2 s); a wait that
+        runs out makes the step give up with status 1 (read_status())."""
         from . import _lib, exl3
         self.layer = layer
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -187,6 +189,7 @@ class EPPeerMoE:
         self._L = L
         g = _lib.EpPeerGroup()
         g.rank, g.world, g.num_global_experts, g.tokens_cap = self.rank, self.world, self.E, self.tokens_cap
+        g.wait_limit_us = int(wait_limit_us)
         self._g = g
         # sizes only depend on the arguments, so every rank computes the same layout
         for d in range(self.world):

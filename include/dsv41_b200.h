@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define DSV41_ABI_VERSION 1
+#define DSV41_ABI_VERSION 2
 
 enum {
     DSV41_OK = 0,
@@ -111,10 +111,17 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
  * process exits. Requests needing more scratch than that fail with DSV41_E_WORKSPACE and a
  * message (at E=384 H=4096 I=2048 top-8 it covers decode batches up to 64 tokens). The first
  * call on a device looks the array up (make it before any stream capture); calls share the array,
- * so calls that overlap on the GPU race. Allocates nothing. */
+ * so calls that overlap on the GPU race. Every argument is checked before anything is queued.
+ * Allocates nothing. The status word of these calls lives in the array: read it with
+ * dsv41_moe_noalloc_read_status, not dsv41_read_status. */
 int dsv41_moe_forward_noalloc(const dsv41_moe_layer* layer, const void* x, int32_t x_dtype, int32_t T,
                               const int64_t* ids, const float* weights, int32_t topk,
                               const dsv41_moe_options* opt, float* out, void* stream);
+/* dsv41_read_status for dsv41_moe_forward_noalloc on the current device (no counterpart in the
+ * reference): synchronise `stream`, return the status word of the library's static scratch (0 = ok,
+ * 1 = a bounded device wait ran out, 3 = more valid routes than options.max_routes) and clear it.
+ * The next dsv41_moe_forward_noalloc call also clears it, so read it after each call you check. */
+int dsv41_moe_noalloc_read_status(void* stream, int32_t* status);
 
 /* Routing permutation (bit-exact, stable by (local expert, flat route index)):
  *   counts/offsets [E+1] int64 (index E = invalid-route sentinel), token_sorted/route_sorted
@@ -207,6 +214,9 @@ typedef struct dsv41_ep_peer_group {
     int32_t num_global_experts;     /* divisible by world */
     int32_t tokens_cap;             /* max tokens per rank and step (same on every rank) */
     void* bases[DSV41_MAX_PEERS];   /* device address of each rank's shared buffer in this process */
+    int32_t wait_limit_us;          /* limit of each wait for the peers' step stamps, 1..2,000,000 us
+                                       (0 = 2 s, the reference combine wait's bound); on expiry the
+                                       step's exchange gives up with status 1 */
 } dsv41_ep_peer_group;
 
 int dsv41_ep_peer_buffer_size(const dsv41_ep_peer_group* group, const dsv41_moe_layer* local_layer, int32_t topk,

@@ -6,10 +6,11 @@ torch.utils.cpp_extension.load and the flags the reference itself uses (ct/ct_vl
 extension runs on whatever host CPU the GPU box has:
   tier_v3  -march=x86-64-v3 (AVX2/FMA/F16C: everything ft_core.h's intrinsics need)
   tier_v4  -march=x86-64-v4 (adds AVX-512; picked at run time when the host supports it)
-Only this container has the reference tree; the GPU box uses the prebuilt .so files.
+Only a machine with the reference tree can run this; machines without it (the GPU box) use the prebuilt .so
+files.
 
 usage: python oracle/build_ref_tier.py [--ref REFERENCE_TREE] [--variants v3,v4]
-(REFERENCE_TREE defaults to $DSV41_REFERENCE, else the checkout location of this build container)
+(REFERENCE_TREE defaults to $DSV41_REFERENCE, else a checkout named `reference` beside this repository)
 """
 import argparse
 import os
@@ -20,7 +21,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("DSV41_REFERENCE", "/root/reference"))
+    sibling = os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    ap.add_argument("--ref", default=os.environ.get("DSV41_REFERENCE", sibling))
     ap.add_argument("--variants", default="v3,v4")
     a = ap.parse_args()
     src = os.path.join(a.ref, "kernels", "cpu_avx2")

@@ -3,10 +3,12 @@
 Each rank holds its shard E/world of a synthetic BASELINE-shape layer and routes its own 64 tokens over
 all global experts; the expert-parallel output (NCCL all-to-all dispatch/combine) must match the
 single-GPU layer (every rank also builds the full layer) within the parity bar; then the same for
-the peer-memory path (EPPeerMoE: token rows and expert outputs read from peers, no collective)."""
+the peer-memory path (EPPeerMoE: token rows and expert outputs read from peers, no collective); last,
+a rank that skips one step makes the other ranks' exchange waits run out (status 1, bounded at 50 ms)."""
 import datetime
 import os
 import sys
+import time
 
 import numpy as np
 import torch
@@ -67,10 +69,45 @@ def main():
         assert_close_layer(out.cpu().numpy(), ref.cpu().numpy(), f"peer rank {rank} case {case}")
     assert peer.read_status() == 0
     peer.close()
+    expired = wait_expiry(shard, full, dev, rank, world)
     dist.barrier()
     print(f"rank {rank}/{world} ok: sent {ep.stats['sent_rows']} rows, received {ep.stats['recv_rows']}; "
-          f"peer steps {peer.stats['steps']}", flush=True)
+          f"peer steps {peer.stats['steps']}; {expired}", flush=True)
     dist.destroy_process_group()
+
+
+def wait_expiry(shard, full, dev, rank, world):
+    """A peer that stays alive but skips a step: the exchange waits of the ranks that did run it give up
+    after the group's 50 ms wait limit with status 1 (the reference counts the same event for its
+    combine wait, ct/ft_tier_cu_v.cu:116-120) and the context stays usable. The failure is made on the
+    host: rank world-1 does not call the step. Every wait in the step is bounded, and no rank leaves
+    while one of its kernels is in flight."""
+    peer = EPPeerMoE(shard, E, tokens_cap=16, topk=K, limit=10.0, wait_limit_us=50000)
+    x = torch.from_numpy(synth.hidden_np(900 + rank, 16, H)).to(dev, torch.bfloat16)
+    ids_np, w_np = synth.routing_np(900 + rank, 16, E, K)
+    ids, w = torch.from_numpy(ids_np).to(dev), torch.from_numpy(w_np).to(dev)
+    ref = exl3.apply_exl3_fused_moe(x, ids, w, full, None, None, 10.0)
+    out = peer(x, ids, w)                                    # step 0: every rank takes part
+    assert peer.read_status() == 0
+    assert_close_layer(out.cpu().numpy(), ref.cpu().numpy(), f"rank {rank} before the skipped step")
+    dist.barrier()
+    skipper = world - 1
+    msg = "skipped step 1"
+    if rank != skipper:
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        out = peer(x, ids, w)                                # step 1: rank `skipper` never arrives
+        status = peer.read_status()
+        dt = time.perf_counter() - t0
+        assert status == 1, status
+        assert 0.05 <= dt < 1.5, dt                          # the 50 ms limit, not the 2 s default
+        assert float(out.abs().max()) == 0.0                 # the gave-up step returns an empty result
+        again = exl3.apply_exl3_fused_moe(x, ids, w, full, None, None, 10.0)
+        assert torch.equal(again, ref)                       # the context is still usable
+        msg = f"exchange wait expired after {dt * 1e3:.0f} ms with status 1"
+    dist.barrier()
+    peer.close()
+    return msg
 
 
 if __name__ == "__main__":

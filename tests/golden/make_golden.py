@@ -1,6 +1,6 @@
 """Generate the golden vectors in tests/golden/ from the REFERENCE's own compiled code.
 
-Runs only where the reference tree has been built into oracle/_ref/ (this dev container):
+Runs only where the reference tree has been built into oracle/_ref/ (a machine with the reference checkout):
   * oracle/_ref/libref_shim.so      kernels/cpu_avx2/ft_core.h compiled unchanged (oracle/Makefile)
   * oracle/_ref/tier_*/ft_tier_host  kernels/cpu_avx2/ft_tier_ext.cpp (oracle/build_ref_tier.py)
 Inputs come from dsv41_flash_offload_b200.synth (seeded, counter-based), so tests regenerate them

@@ -1,4 +1,5 @@
-"""Expert parallelism on real GPUs: NCCL all-to-all dispatch/combine vs the single-GPU layer
+"""Expert parallelism on real GPUs: NCCL all-to-all dispatch/combine and the peer-memory exchange vs the
+single-GPU layer, and a skipped step that makes the peers' bounded exchange waits run out (status 1)
 (tests/ep_worker.py under torchrun, one rank per visible GPU, 2 to 8). Skipped with one GPU."""
 import os
 import socket
@@ -32,3 +33,4 @@ def test_ep_nccl_matches_single_gpu():
     r = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert r.stdout.count(" ok: ") == n
+    assert r.stdout.count("exchange wait expired after") == n - 1

@@ -117,7 +117,7 @@ def test_capi_library_exports_every_declared_symbol():
     assert set(declared) == set(_lib.SYMBOLS)
     for name in declared:
         assert hasattr(L, name), name
-    assert L.dsv41_abi_version() == 1
+    assert L.dsv41_abi_version() == _lib.ABI_VERSION == 2
     assert b"sm_100a" in L.dsv41_build_info()
 
 
@@ -209,6 +209,15 @@ def test_ep_peer_buffer_layout_host_checks():
     assert size(2, 2, 64)[0] == _lib.E_INVALID           # rank out of range
     assert size(5, 0, 64, E=384)[0] == _lib.E_INVALID    # 384 experts do not shard over 5
     assert size(2, 0, 0)[0] == _lib.E_INVALID            # no capacity
+    g = _lib.EpPeerGroup()
+    g.rank, g.world, g.num_global_experts, g.tokens_cap = 0, 2, 384, 64
+    for d in range(_lib.MAX_PEERS):
+        g.bases[d] = 16
+    lay = _lib.MoeLayer(192, 4096, 2048, 0, *([16] * 7))
+    n = C.c_size_t()
+    for lim, want in ((0, 0), (50000, 0), (2000000, 0), (-1, _lib.E_INVALID), (2000001, _lib.E_INVALID)):
+        g.wait_limit_us = lim                             # exchange wait bound: 0 = 2 s, else 1 us .. 2 s
+        assert L.dsv41_ep_peer_buffer_size(C.byref(g), C.byref(lay), 8, 32, C.byref(n)) == want, lim
     del layer
 
 

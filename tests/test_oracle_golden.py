@@ -92,7 +92,7 @@ def test_layer_c0_matches_reference(oracle):
 
 
 def test_oracle_against_local_reference_build(oracle):
-    """Direct pin where oracle/_ref was built from the reference tree (dev container)."""
+    """Direct pin where oracle/_ref was built from the reference tree (machines with the reference checkout)."""
     from oracle.oracle import RefShim
     if not RefShim.available():
         pytest.skip("oracle/_ref not built here")
