@@ -43,17 +43,22 @@ def needs_build() -> bool:
     return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
 
 
-def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = False) -> str:
-    if not force and not needs_build():
+def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = False, defines=(),
+          lib_path: str = LIB) -> str:
+    """Build the library (when a source is newer than it, or `force`). `defines` are extra -D flags
+    (the kernels' compile-time launch-shape switches) and `lib_path` the output, for variants."""
+    if not force and lib_path == LIB and not defines and not needs_build():
         return LIB
     from concurrent.futures import ThreadPoolExecutor
 
     nvcc = nvcc_path()
     ver = nvcc_version(nvcc)
-    flags = [*ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", f'-DDSV41_NVCC_VERSION="{ver}"']
+    flags = [*ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", f'-DDSV41_NVCC_VERSION="{ver}"',
+             *[f"-D{d}" for d in defines]]
     if ptxas_verbose:
         flags.insert(0, "-Xptxas=-v")
-    objdir = os.path.join(HERE, "_build")
+    tag = os.path.splitext(os.path.basename(lib_path))[0]
+    objdir = os.path.join(HERE, "_build", tag)
     os.makedirs(objdir, exist_ok=True)
 
     def compile_one(src):
@@ -72,13 +77,13 @@ def build(verbose: bool = False, force: bool = False, ptxas_verbose: bool = Fals
             raise RuntimeError("nvcc failed building libdsv41_b200.so")
         if verbose or ptxas_verbose:
             sys.stderr.write(r.stderr)
-    link = [nvcc, *ARCH, "-shared", "-cudart", "static", "-o", LIB + ".tmp"] + [o for o, _ in results]
+    link = [nvcc, *ARCH, "-shared", "-cudart", "static", "-o", lib_path + ".tmp"] + [o for o, _ in results]
     r = subprocess.run(link, capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)
         raise RuntimeError("nvcc failed linking libdsv41_b200.so")
-    os.replace(LIB + ".tmp", LIB)
-    return LIB
+    os.replace(lib_path + ".tmp", lib_path)
+    return lib_path
 
 
 if __name__ == "__main__":

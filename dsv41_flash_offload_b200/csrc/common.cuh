@@ -161,6 +161,43 @@ __device__ __forceinline__ void decode_tile(const uint32_t* tw, const LaneDec<K>
 }
 
 // ------------------------------------------------------------------------------------------
+// Affine form of the same decode (the reference CPU tier's AFFINE mode, ft_core.h:293 and its
+// mode choice :936): w = KINV * code + KBIAS with code = 1024 + bytesum, so for any activations x
+//   sum_k w_k x_k = KINV * sum_k code_k x_k + KBIAS * sum_k x_k   (exact in real arithmetic).
+// The fragments then carry the codes themselves (fp16 1024..2044, exact) and the per-weight
+// HFMA2 is gone; the caller applies KINV / KBIAS to the fp32 sums. It skips only the fp16 rounding
+// of each weight (a half-ulp, 2^-11 relative). `kImadPacks` of the 4 half2 packs per lane go to the
+// IMAD pipe (c1 * 65536 + c0), the rest to PRMT, to balance the two integer pipes.
+// ------------------------------------------------------------------------------------------
+constexpr float kKinv = 0.00676727294921875f;   // fp16 0x1eee = 1774 * 2^-18 (exact)
+constexpr float kKbias = -10.3828125f;          // fp16 0xc931 = -1329 * 2^-7 (exact)
+
+template <int K, int kImadPacks = 2>
+__device__ __forceinline__ void decode_tile_codes(const uint32_t* tw, const LaneDec<K>& d, uint32_t k16,
+                                                  uint32_t (&b)[4])
+{
+    uint32_t s[8];
+    if constexpr (K == 3) {
+        const uint32_t hi = __funnelshift_l(tw[d.q1], tw[d.q0], d.r);
+        const uint32_t lo = __funnelshift_l(tw[d.q2], tw[d.q1], d.r);
+#pragma unroll
+        for (int j = 0; j < 5; ++j) s[j] = __funnelshift_r(lo, hi, 29 - 3 * j) & 0xffffu;
+        s[5] = (lo >> 14) & 0xffffu;
+        s[6] = (lo >> 11) & 0xffffu;
+        s[7] = __byte_perm(lo, 0u, 0x4421);
+    } else {
+        const uint32_t hi = tw[d.q0], lo = tw[d.q1];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s[j] = __funnelshift_r(lo, hi, d.r - K * j) & 0xffffu;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+        const uint32_t c0 = state_code(s[j]), c1 = state_code(s[j + 1]);
+        b[j >> 1] = (j / 2 < kImadPacks) ? c1 * k16 + c0 : __byte_perm(c0, c1, 0x5410);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
 // fp16 rounding helper and the 128-point Walsh-Hadamard transform over a warp
 // (lane holds elements lane*4 + q, q = 0..3; stage order w = 1, 2, 4, ..., 64 as the reference's
 // had128, ft_core.h:89-94, so every fp32 intermediate is the same)

@@ -13,10 +13,19 @@
 //             k-row segment and per 256-byte activation row into a 2-stage mbarrier ring of 16
 //             k-rows per stage; trellis reads carry an L2 evict-first hint (each expert byte is
 //             read once).
-//   consumer warp w: owns two adjacent 16-column n-tiles that share one ldmatrix'd A fragment;
-//             per k-tile and n-tile it loads the window words of its lane from the staged tile,
-//             decodes its 8 weights into two mma B fragments in registers, and issues two
-//             mma.m16n8k16 (rows = tokens). Decoded weights never leave registers.
+//   consumer warp w: owns two adjacent 16-column n-tiles that share one ldmatrix'd fragment of the
+//             group's tokens; per k-tile and n-tile it loads the window words of its lane from the
+//             staged tile, decodes its 8 weights in registers and issues mma.m16n8k16 with the
+//             decoded tile as the A operand (16 features x 16 k) and the tokens as the B operand
+//             (k16 x n8): one MMA per tile for groups of up to 8 rows, two for 9-16. The lane's 8
+//             symbols are the mma fragment's (k, n) pairs in either operand role (the format is laid
+//             out for it), only the register order differs. Decoded weights never leave registers.
+//   affine form (DSV41_GEMV_AFFINE, default): the A fragments carry the weights' affine codes
+//             1024 + bytesum (decode_tile_codes), one more MMA per k-row against an all-ones A
+//             gives the token sums, and the epilogue forms KINV * sum(code x) + KBIAS * sum(x) in
+//             fp32 -- the reference CPU tier's AFFINE mode (kernels/cpu_avx2/ft_core.h:293, chosen
+//             by its auto mode at decode sizes, :936). It differs from the exact form (fp16-rounded
+//             weights, DSV41_GEMV_AFFINE=0) by the weights' fp16 rounding only.
 // Split-K partials (small batches) are reduced in a fixed order by the last-arriving CTA, so
 // results are deterministic.
 #include "common.cuh"
@@ -34,8 +43,18 @@ namespace dsv41 {
 #ifndef DSV41_GEMV_STAGES
 #define DSV41_GEMV_STAGES 2
 #endif
-// Measured on B200, decode T=64 step: (1 tile/warp, 8 rows, 4 stages) 2.12 ms; (1, 16, 2) 1.98;
-// (2, 8, 4) 1.97; (2, 16, 2) 1.88; 1 CTA/SM or 3 CTAs/SM variants were slower.
+// Measured on B200 (gate/up GEMV of the decode T=64 step, 285 experts): tokens as the A operand
+// (two MMAs per tile) with exact weights 1.217 ms; the same with affine codes 1.177; weights as the A
+// operand, exact 1.122, affine 1.102 (kept). Not kept: byte sums on the tensor pipe (two int8 MMAs per
+// tile instead of 8 DP4A) 1.279; one tile per warp (16 consumer warps) 1.277; 3 CTAs/SM with 8-row
+// stages 1.147; 8-row stages x 4 1.176. Earlier: 16-row stages x 2 beat 8 x 4 and 1 or 3 CTAs/SM.
+
+#ifndef DSV41_GEMV_AFFINE
+#define DSV41_GEMV_AFFINE 1
+#endif
+#ifndef DSV41_GEMV_IMAD_PACKS
+#define DSV41_GEMV_IMAD_PACKS 4       // of the 4 half2 code packs per lane and tile, how many on IMAD
+#endif
 
 #ifndef DSV41_GEMV_TILES_PER_WARP
 #define DSV41_GEMV_TILES_PER_WARP 2   // adjacent n-tiles per consumer warp (they share the A fragment)
@@ -79,6 +98,49 @@ __device__ __forceinline__ void out_block4(float (&y)[4], const __half* svh, int
     const float s[4] = {__low2float(a), __high2float(a), __low2float(b), __high2float(b)};
 #pragma unroll
     for (int q = 0; q < 4; ++q) y[q] = r16(__fmul_rn(__fmul_rn(y[q], kHad), s[q]));
+}
+
+__device__ __forceinline__ void ldmatrix_x2(uint32_t (&a)[4], uint32_t addr)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(a[0]), "=r"(a[1]) : "r"(addr));
+}
+
+// One staged k-row block: for each k-row, the tokens' B fragments (TWO: tokens 8-15 as a second n8
+// block), then per tile the decoded A fragment {b0, b2, b1, b3} (decode_tile returns the lane's
+// weights in B-fragment register order: (k 2q.., n g), (k 2q+8.., n g), (k 2q.., n g+8), (k 2q+8..,
+// n g+8)) and one MMA per n8 block. The affine form adds the token sums from an all-ones A.
+template <int K, bool TWO>
+__device__ __forceinline__ void gemv_stage(const uint32_t* trow, uint32_t xaddr, const LaneDec<K>& lw,
+                                                   uint32_t k16, float (&acc)[kTilesPerWarp][2][4],
+                                                   float (&rs)[2][4])
+{
+    constexpr int kTW = TileFmt<K>::words, kRowWords = row_bytes<K>() / 4;
+#pragma unroll
+    for (int r = 0; r < kStageRows; ++r) {
+        uint32_t bx[4];
+        if (TWO)
+            ldmatrix_x4(bx, xaddr + r * 32);
+        else
+            ldmatrix_x2(bx, xaddr + r * 32);
+#if DSV41_GEMV_AFFINE
+        const uint32_t ones[4] = {0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u};
+        mma_16816(rs[0], ones, bx[0], bx[1]);
+        if (TWO) mma_16816(rs[1], ones, bx[2], bx[3]);
+#endif
+#pragma unroll
+        for (int t = 0; t < kTilesPerWarp; ++t) {
+            const uint32_t* tw = trow + r * kRowWords + t * kTW;
+            uint32_t b[4];
+#if DSV41_GEMV_AFFINE
+            decode_tile_codes<K, DSV41_GEMV_IMAD_PACKS>(tw, lw, k16, b);
+#else
+            decode_tile<K>(tw, lw, k16, b);
+#endif
+            const uint32_t a[4] = {b[0], b[2], b[1], b[3]};
+            mma_16816(acc[t][0], a, bx[0], bx[1]);
+            if (TWO) mma_16816(acc[t][1], a, bx[2], bx[3]);
+        }
+    }
 }
 
 template <int MODE, int K>
@@ -166,7 +228,8 @@ __global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv
     const uint32_t k16 = p.k16;
     const int tile0 = warp * kTilesPerWarp;       // first of this warp's adjacent n-tiles (0..15)
     const int mat = MODE == 0 ? (tile0 >> 3) : 0;  // gate/up pass: tiles 0-7 gate, 8-15 up
-    const uint32_t x_lane = ((lane & 7) + ((lane >> 3) & 1) * 8) * kXRowStride + ((lane >> 4) & 1) * 16;
+    // B fragments: matrices (tokens 0-7, k 0-7), (0-7, 8-15), (8-15, 0-7), (8-15, 8-15)
+    const uint32_t x_lane = ((lane & 7) + ((lane >> 4) & 1) * 8) * kXRowStride + ((lane >> 3) & 1) * 16;
     uint32_t it = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
         const int ucb = u / p.split, cb = ucb % n_cb, g = ucb / n_cb;
@@ -179,6 +242,8 @@ __global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv
             for (int h = 0; h < 2; ++h)
 #pragma unroll
                 for (int q = 0; q < 4; ++q) acc[t][h][q] = 0.f;
+        float rs[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};   // token sums (affine form)
+        const bool two = rows > 8;
         for (int st = 0; st < stages_per_unit; ++st, ++it) {
             const int stage = it % kStages;
             const uint32_t round = it / kStages;
@@ -188,35 +253,39 @@ __global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv
                 // this warp's tiles sit at byte offset tile * 32K of each staged 16-tile k-row
                 const uint32_t* trow = reinterpret_cast<const uint32_t*>(S.tr[stage]) + tile0 * kTW;
                 const uint32_t xaddr = smem_addr(S.x[stage][mat]) + x_lane;
-#pragma unroll
-                for (int r = 0; r < kStageRows; ++r) {
-                    uint32_t a[4];
-                    ldmatrix_x4(a, xaddr + r * 32);
-#pragma unroll
-                    for (int t = 0; t < kTilesPerWarp; ++t) {
-                        const uint32_t* tw = trow + r * (kRowBytes / 4) + t * kTW;
-                        uint32_t b[4];
-                        decode_tile<K>(tw, lw, k16, b);
-                        mma_16816(acc[t][0], a, b[0], b[1]);
-                        mma_16816(acc[t][1], a, b[2], b[3]);
-                    }
-                }
+                if (two)
+                    gemv_stage<K, true>(trow, xaddr, lw, k16, acc, rs);
+                else
+                    gemv_stage<K, false>(trow, xaddr, lw, k16, acc, rs);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[stage]);
         }
 
-        // accumulators -> shared [mat][row][cols]
+#if DSV41_GEMV_AFFINE
+        // sum_k w x = KINV * sum_k code x + KBIAS * sum_k x (per split: the partial sums add up the same)
+#pragma unroll
+        for (int t = 0; t < kTilesPerWarp; ++t)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[t][h][q] = fmaf(kKinv, acc[t][h][q], kKbias * rs[h][q]);
+#endif
+        // accumulators (feature g / g + 8 of the tile, tokens 8h + 2q, + 1) -> shared [mat][row][cols]
 #pragma unroll
         for (int t = 0; t < kTilesPerWarp; ++t) {
             const int tile = tile0 + t;
-            const int tcol = (MODE == 0 ? (tile & 7) : tile) * 16 + (lane & 3) * 2;
-            const int r = lane >> 2;
+            const int fcol = (MODE == 0 ? (tile & 7) : tile) * 16 + (lane >> 2);
             float* ep = S.ep + (MODE == 0 ? mat * 16 * cols : 0);
-            *reinterpret_cast<float2*>(ep + r * cols + tcol) = make_float2(acc[t][0][0], acc[t][0][1]);
-            *reinterpret_cast<float2*>(ep + (r + 8) * cols + tcol) = make_float2(acc[t][0][2], acc[t][0][3]);
-            *reinterpret_cast<float2*>(ep + r * cols + tcol + 8) = make_float2(acc[t][1][0], acc[t][1][1]);
-            *reinterpret_cast<float2*>(ep + (r + 8) * cols + tcol + 8) = make_float2(acc[t][1][2], acc[t][1][3]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (h == 1 && !two) break;
+                const int tok = 8 * h + (lane & 3) * 2;
+                ep[tok * cols + fcol] = acc[t][h][0];
+                ep[(tok + 1) * cols + fcol] = acc[t][h][1];
+                ep[tok * cols + fcol + 8] = acc[t][h][2];
+                ep[(tok + 1) * cols + fcol + 8] = acc[t][h][3];
+            }
         }
         named_bar_sync(1, kConsumerWarps * 32);
 
