@@ -139,6 +139,13 @@ static T* at(void* ws, size_t off)
     return reinterpret_cast<T*>(static_cast<uint8_t*>(ws) + off);
 }
 
+// where the row transform leaves the rows' input sums for the busy-expert GEMM (its affine weight codes),
+// or NULL when no expert of the call can take the GEMM path
+static float* gemm_sums(void* ws, const Layout& L, int fat)
+{
+    return (fat >= 0 && L.rows > fat) ? gemm_row_sums(at<uint8_t>(ws, L.gemm), L.rows, L.E) : nullptr;
+}
+
 static PermBuffers perm_buffers(void* ws, const Layout& L)
 {
     PermBuffers pb{};
@@ -433,7 +440,8 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     __half* xt_d = at<__half>(workspace, L.xt_d);
     __half* y = at<__half>(workspace, L.y);
     if ((err = launch_prep(x, x_dtype, pb.token_sorted, pb.expert_sorted, pb.nrows, L.rows,
-                           static_cast<const __half*>(layer->w13_suh), H, xt_g, xt_u, st)) != cudaSuccess)
+                           static_cast<const __half*>(layer->w13_suh), H, xt_g, xt_u,
+                           gemm_sums(workspace, L, fat), st)) != cudaSuccess)
         return cuda_fail(err, "prep");
     timer_mark(st, 2);
     if ((err = run_expert_passes(layer, pb, xt_g, xt_u, xt_d, y, at<float>(workspace, L.partials),
@@ -523,6 +531,7 @@ int dsv41_ep_peer_forward(const dsv41_moe_layer* local_layer, const dsv41_ep_pee
     if (local_layer->num_experts != e_loc)
         return fail(DSV41_E_INVALID, "local layer has %d experts, expected %d", local_layer->num_experts, e_loc);
     if (T < 0 || T > tcap || k <= 0) return fail(DSV41_E_INVALID, "T=%d (tokens_cap %d), topk=%d", T, tcap, k);
+    if (H > 8192) return fail(DSV41_E_INVALID, "expert-parallel peer path supports hidden <= 8192, got %d", H);
     if (x_dtype < DSV41_DTYPE_F16 || x_dtype > DSV41_DTYPE_F32) return fail(DSV41_E_INVALID, "bad x_dtype %d", x_dtype);
     if (T > 0 && (!x || !ids || !weights || !out)) return fail(DSV41_E_INVALID, "NULL input/output pointer");
     if ((rc = check_alignment(x, out, nullptr))) return rc;
@@ -565,7 +574,7 @@ int dsv41_ep_peer_forward(const dsv41_moe_layer* local_layer, const dsv41_ep_pee
     xr.n = world;
     if ((err = launch_prep_rows(xr, DSV41_DTYPE_F16, pb.token_sorted, pb.expert_sorted, pb.nrows, L.rows,
                                 static_cast<const __half*>(local_layer->w13_suh), H, at<__half>(ws, L.xt_g),
-                                at<__half>(ws, L.xt_u), st)) != cudaSuccess)
+                                at<__half>(ws, L.xt_u), gemm_sums(ws, L, fat), st)) != cudaSuccess)
         return cuda_fail(err, "prep");
     timer_mark(st, 2);
     if ((err = run_expert_passes(local_layer, pb, at<__half>(ws, L.xt_g), at<__half>(ws, L.xt_u),
@@ -831,8 +840,9 @@ int dsv41_expert_gemm(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     __half* xt_u = at<__half>(workspace, offs[8]);
     __half* xt_d = at<__half>(workspace, offs[9]);
     __half* y = at<__half>(workspace, offs[10]);
+    float* rsum = total_rows > fat ? gemm_row_sums(at<uint8_t>(workspace, offs[13]), total_rows, n_experts) : nullptr;
     if ((err = launch_prep(x, x_dtype, token_sorted, pb.expert_sorted, nrows, total_rows,
-                           static_cast<const __half*>(layer->w13_suh), H, xt_g, xt_u, st)) != cudaSuccess)
+                           static_cast<const __half*>(layer->w13_suh), H, xt_g, xt_u, rsum, st)) != cudaSuccess)
         return cuda_fail(err, "prep");
     if ((err = run_expert_passes(layer, pb, xt_g, xt_u, xt_d, y, at<float>(workspace, offs[11]),
                                  at<int>(workspace, offs[12]), at<int>(workspace, offs[0]), split, gb, total_rows, limit,

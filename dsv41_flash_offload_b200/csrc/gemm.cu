@@ -113,6 +113,8 @@ struct GemmParams {
     const __half* svh_a;    // gate/up: w13_svh [E][2][N]; down: w2_svh [E][N]
     const __half* suh_d;    // gate/up: w2_suh [E][N]
     __half* out;            // gate/up: xt_d [rows][N]; down: y [rows][N]
+    const float* rs;        // activation sums per sorted row: gate/up [2 rows] (gate, up); down [rows][K/128]
+    float* xs_out;          // gate/up: block sums of the stored down inputs [rows][N/128]
     int* status;
     int K, N;
     float limit;
@@ -203,6 +205,13 @@ __device__ __forceinline__ void st_global_32B(void* p, const uint32_t (&o)[8])
                  : "memory");
 }
 
+__device__ __forceinline__ void stmatrix_x4(uint32_t addr, const uint32_t (&r)[4])
+{
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3])
+                 : "memory");
+}
+
 __device__ __forceinline__ void load_half8(const __half* p, float* dst)
 {
     const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
@@ -233,21 +242,24 @@ __device__ __forceinline__ void out_block128(float (&v)[128], const __half* svh)
 }
 
 // gate/up epilogue of one row and one 128-feature block (accumulators at TMEM columns tg / tu of this
-// thread's lane): v = H128(fp16(act(out_block(g), out_block(u))) * suh_d) * HAD, the down-input row
-// before its fp16 rounding. Intermediate blocks are parked in TMEM, 32 columns at a time, so no more
-// than 128 + 64 values are live in registers.
+// thread's lane, sums of the affine weight codes times the inputs): g = KINV * acc_g + bias_g (bias =
+// KBIAS * the row's input sum), likewise u; v = H128(fp16(act(out_block(g), out_block(u))) * suh_d) *
+// HAD, the down-input row before its fp16 rounding. Intermediate blocks are parked in TMEM, 32 columns
+// at a time, so no more than 128 + 64 values are live in registers.
 __device__ __forceinline__ void gateup_epilogue(float (&v)[128], uint32_t tg, uint32_t tu, const __half* svg,
-                                                const __half* svu, const __half* sd, float limit)
+                                                const __half* svu, const __half* sd, float limit, float bias_g,
+                                                float bias_u)
 {
 #pragma unroll 1
     for (int m = 0; m < 2; ++m) {
         const uint32_t col = m ? tu : tg;
+        const float bias = m ? bias_u : bias_g;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             float t[32];
             tmem_ld32(col + q * 32, t);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[q * 32 + i] = t[i];
+            for (int i = 0; i < 32; ++i) v[q * 32 + i] = fmaf(kKinv, t[i], bias);
         }
         out_block128(v, m ? svu : svg);
 #pragma unroll
@@ -511,7 +523,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
         const int d = warp - kWarpDec0;               // 0..7
         const LaneDec<K> lw = lane_dec_setup<K>(lane);
         const uint32_t k16 = p.k16;
-        const int r0 = (lane & 3) * 2, c0 = lane >> 2;
         // decode assignment: the chunk's nmat * kKT (matrix, k-tile) rows of 8 n-tiles are split
         // evenly over the 8 decoder warps (wpg warps per row, ntn adjacent n-tiles each)
         constexpr int wpg = kDecWarps / (Cfg::nmat * kKT);
@@ -519,16 +530,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
         const int grp = d / wpg;
         const int dmat = grp / kKT, dkt = grp % kKT;
         const int nt0 = (d % wpg) * ntn;
-        // byte offsets of this lane's four B words inside one 16-column n-tile of the swizzled
-        // K-major operand: element (n, k) at (n/8)*kAtom + (n%8)*kRowB + ((k/8) ^ sw(n%8))*16 + (k%8)*2,
-        // sw(r) = r for the 128-byte swizzle and r/2 for the 64-byte one
-        uint32_t boff[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int n = c0 + ((q >> 1) << 3);
-            const int k = dkt * 16 + r0 + ((q & 1) << 3);
+        // One stmatrix.x4 per tile stores the lane's four fragment registers: matrix q holds features
+        // n = 8 (q >> 1) + 0..7 and k = 8 (q & 1) + 0..7 of the tile (register q of every lane, rows as
+        // the mma fragment), and lane i gives the address of row i % 8 of matrix i / 8. In the swizzled
+        // K-major operand, element (n, k) sits at (n/8)*kAtom + (n%8)*kRowB + ((k/8) ^ sw(n%8))*16 +
+        // (k%8)*2, sw(r) = r for the 128-byte swizzle and r/2 for the 64-byte one, so each matrix row
+        // is one 16-byte chunk.
+        uint32_t soff;
+        {
+            const int q = lane >> 3, n = (lane & 7) + ((q >> 1) << 3);
+            const int kc = dkt * 2 + (q & 1);   // 16-byte chunk index of the row within the stage
             const int sw = kBK == 64 ? (n & 7) : ((n & 7) >> 1);
-            boff[q] = (uint32_t)((n >> 3) * kAtom + (n & 7) * kRowB + (((k >> 3) ^ sw) * 16) + (k & 7) * 2);
+            soff = (uint32_t)((n >> 3) * kAtom + (n & 7) * kRowB + ((kc ^ sw) * 16));
         }
         const int quarter = warp & 3;                 // TMEM lanes this warp may access
         uint32_t it = 0, ib = 0, units_done = 0;
@@ -546,14 +559,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                     break;
                 }
                 const uint32_t* trw = reinterpret_cast<const uint32_t*>(stage_t(st, dmat, dkt));
-                uint8_t* bt = stage_b(sb, dmat) + nt0 * 2 * kAtom;
+                const uint32_t bt = smem_addr(stage_b(sb, dmat) + nt0 * 2 * kAtom) + soff;
 #pragma unroll kDecUnroll
                 for (int j = 0; j < ntn; ++j) {
                     const uint32_t* tw = trw + (nt0 + j) * TileFmt<K>::words;
                     uint32_t b[4];
-                    decode_tile<K>(tw, lw, k16, b);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) *reinterpret_cast<uint32_t*>(bt + j * 2 * kAtom + boff[q]) = b[q];
+                    decode_tile_codes<K, 4>(tw, lw, k16, b);   // affine codes: the epilogue applies KINV, KBIAS
+                    stmatrix_x4(bt + j * 2 * kAtom, b);
                 }
                 fence_async_smem();
                 __syncwarp();
@@ -583,16 +595,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
                 if (mt * kBM >= rows) continue;  // whole M tile empty (warp-uniform)
                 float v[128];
+                // the row's input sum(s) of the affine form (rows past the pass are never stored)
+                const bool live = row < rows;
+                const size_t grow = (size_t)(row0 + row);
                 if (MODE == 0) {
                     const uint32_t colg = (uint32_t)((mt * 2 + 0) * kBN), colu = (uint32_t)((mt * 2 + 1) * kBN);
                     const __half* svg = p.svh_a + (size_t)e * 2 * p.N + fb * kBN;
+                    const float2 rs = live ? *reinterpret_cast<const float2*>(p.rs + 2 * grow) : make_float2(0.f, 0.f);
                     gateup_epilogue(v, lane_addr + colg, lane_addr + colu, svg, svg + p.N,
-                                    p.suh_d + (size_t)e * p.N + fb * kBN, p.limit);
+                                    p.suh_d + (size_t)e * p.N + fb * kBN, p.limit, kKbias * rs.x, kKbias * rs.y);
+                    if (live) {   // block sum of the stored down inputs (the down pass's affine form)
+                        float bs = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < 128; ++i) bs += r16(v[i]);
+                        p.xs_out[grow * (p.N / kBN) + fb] = bs;
+                    }
                 } else {
+                    float xs = 0.0f;
+                    if (live)
+                        for (int b = 0; b < p.K / 128; ++b) xs += p.rs[grow * (p.K / 128) + b];
                     tmem_ld128(lane_addr + (uint32_t)(mt * kBN), v);
+#pragma unroll
+                    for (int i = 0; i < 128; ++i) v[i] = fmaf(kKinv, v[i], kKbias * xs);
                     out_block128(v, p.svh_a + (size_t)e * p.N + fb * kBN);
                 }
-                if (row < rows) {
+                if (live) {
                     // 256 B of the row as eight 32-byte stores (rows are 4-8 KB, blocks 256 B: 32-byte aligned)
                     __half* dst = p.out + (size_t)(row0 + row) * p.N + fb * kBN;
 #pragma unroll
@@ -636,9 +663,25 @@ __global__ void gemm_plan_kernel(const int* fat_experts, const int* n_fat, const
 // passes = sum over busy experts of ceil(rows / rp) <= N / rp + (number of experts, <= min(N, kMaxExperts))
 static int max_passes(int N, int /*E*/, int rp) { return N / rp + (N < kMaxExperts ? N : kMaxExperts) + 1; }
 
+static size_t pass_list_bytes(int N, int E)
+{
+    return (size_t)(max_passes(N, E, GemmCfg<0, 3>::rows_per_pass) + max_passes(N, E, GemmCfg<1, 3>::rows_per_pass)) * 16;
+}
+
 size_t gemm_scratch_bytes(int N, int E, int H, int I)
 {
-    return (size_t)(max_passes(N, E, GemmCfg<0, 3>::rows_per_pass) + max_passes(N, E, GemmCfg<1, 3>::rows_per_pass)) * 16 + 256;
+    const size_t n = (size_t)(N > 0 ? N : 1);
+    return 256 + pass_list_bytes(N, E) + (2 * n + n * (size_t)(I / 128)) * 4;
+}
+
+float* gemm_row_sums(uint8_t* scratch, int N, int E)
+{
+    return reinterpret_cast<float*>(scratch + 256 + pass_list_bytes(N, E));
+}
+
+float* gemm_down_sums(uint8_t* scratch, int N, int E)
+{
+    return gemm_row_sums(scratch, N, E) + 2 * (size_t)(N > 0 ? N : 1);
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
@@ -697,6 +740,8 @@ static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
         p.svh_a = static_cast<const __half*>(a.layer->w13_svh);
         p.suh_d = static_cast<const __half*>(a.layer->w2_suh);
         p.out = a.xt_d;
+        p.rs = gemm_row_sums(a.scratch, N, E);
+        p.xs_out = gemm_down_sums(a.scratch, N, E);
         p.K = H;
         p.N = I;
     } else {
@@ -709,6 +754,8 @@ static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
         p.svh_a = static_cast<const __half*>(a.layer->w2_svh);
         p.suh_d = nullptr;
         p.out = a.y;
+        p.rs = gemm_down_sums(a.scratch, N, E);
+        p.xs_out = nullptr;
         p.K = I;
         p.N = H;
     }

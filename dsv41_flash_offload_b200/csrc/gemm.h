@@ -27,7 +27,12 @@ struct GemmArgs {
     int* status;
 };
 
+// GEMM scratch (N = row bound, E = experts): pass counters and lists, then the per-row activation sums
+// of the affine weight codes -- gemm_row_sums [2 N] (gate, up; written by the row transform) and
+// gemm_down_sums [N][I / 128] (block sums of the down inputs; written by the gate/up epilogue)
 size_t gemm_scratch_bytes(int N, int E, int H, int I);
+float* gemm_row_sums(uint8_t* scratch, int N, int E);
+float* gemm_down_sums(uint8_t* scratch, int N, int E);
 cudaError_t launch_gemm_gateup(const GemmArgs& a, cudaStream_t st);
 cudaError_t launch_gemm_down(const GemmArgs& a, cudaStream_t st);
 

@@ -52,15 +52,16 @@ cudaError_t launch_permute(const int64_t* ids, const float* weights, int N, int 
                            const int32_t* expert_map, int map_len, int fat_threshold,
                            const PermBuffers& pb, cudaStream_t st);
 
+// rsum (optional, [2 * N] fp32): per sorted row, the sums of the row's stored xt_g / xt_u values
 cudaError_t launch_prep(const void* x, int x_dtype, const int* token_sorted, const int* expert_sorted,
                         const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
-                        cudaStream_t st);
+                        float* rsum, cudaStream_t st);
 cudaError_t launch_router_topk(const void* logits, int logits_dtype, int T, int E, int k, int scoring,
                                int renormalize, int n_group, int topk_group, const float* bias, float scale,
                                int64_t* ids, float* w, cudaStream_t st);
 cudaError_t launch_prep_rows(const XRows& x, int x_dtype, const int* token_sorted, const int* expert_sorted,
                              const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
-                             cudaStream_t st);
+                             float* rsum, cudaStream_t st);
 cudaError_t launch_ep_publish(const void* x, int x_dtype, const int64_t* ids, const float* w, int T, int tcap, int k,
                               int E, int H, __half* X, int* IDS, float* W, cudaStream_t st);
 cudaError_t launch_ep_signal(const PeerTable& peers, int world, int rank, size_t flag_off, uint32_t stamp,

@@ -88,10 +88,13 @@ __device__ __forceinline__ void had128_quad(float (&v)[32], int hl)
 // one warp per sorted row p (rows p < *nrows; rows whose expert_sorted entry is negative are skipped):
 // lanes 4g .. 4g+3 transform 128-block 8j + g of the row for gate and up,
 //   xt_{g,u}[p] = fp16(H128(fp16(x[token]) * suh_{g,u}) * 2^-3.5)
-// with 16-byte loads and stores; the row's indices are read once
+// with 16-byte loads and stores; the row's indices are read once. With rsum, it also writes the sums of
+// the stored (fp16) values of the row, rsum[2p] (gate) and rsum[2p + 1] (up), in fp32 in a fixed order:
+// the activation sums of the busy-expert GEMM's affine weight codes.
 __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ XRows x, int x_dtype, const int* token_sorted,
                                                    const int* expert_sorted, const int* nrows,
-                                                   const __half* w13_suh, int H, __half* xt_g, __half* xt_u)
+                                                   const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
+                                                   float* rsum)
 {
     const int lane = threadIdx.x & 31, hl = lane & 3, g = lane >> 2;
     const int nvalid = *nrows;
@@ -109,6 +112,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ XRows
             row = (size_t)(t % x.per);
         }
         const __half* sg = w13_suh + (size_t)e * 2 * H;
+        float sum[2] = {0.0f, 0.0f};
         for (int j = 0; j < nit; ++j) {
             const int blk = 8 * j + g;
             const bool act = blk < nb;   // lanes past the last block transform a copy of block 0, unstored
@@ -138,34 +142,45 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ XRows
                     float w8[8];
 #pragma unroll
                     for (int q = 0; q < 8; ++q) w8[q] = __fmul_rn(v[8 * k + q], kHad);
-                    if (act) store8_half(o + 8 * k, w8);
+                    if (act) {
+                        store8_half(o + 8 * k, w8);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) sum[m] += r16(w8[q]);
+                    }
                 }
             }
+        }
+        if (rsum) {
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) sum[m] += __shfl_xor_sync(0xffffffffu, sum[m], o);
+            if (lane == 0) *reinterpret_cast<float2*>(rsum + 2 * (size_t)p) = make_float2(sum[0], sum[1]);
         }
     }
 }
 
 cudaError_t launch_prep(const void* x, int x_dtype, const int* token_sorted, const int* expert_sorted,
                         const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
-                        cudaStream_t st)
+                        float* rsum, cudaStream_t st)
 {
     XRows xr{};
     xr.base[0] = x;
     xr.per = 1;
     xr.n = 1;
-    return launch_prep_rows(xr, x_dtype, token_sorted, expert_sorted, nrows, N, w13_suh, H, xt_g, xt_u, st);
+    return launch_prep_rows(xr, x_dtype, token_sorted, expert_sorted, nrows, N, w13_suh, H, xt_g, xt_u, rsum, st);
 }
 
 cudaError_t launch_prep_rows(const XRows& x, int x_dtype, const int* token_sorted, const int* expert_sorted,
                              const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
-                             cudaStream_t st)
+                             float* rsum, cudaStream_t st)
 {
     long long blocks = ((long long)N + 7) / 8;   // one warp per sorted row
     const long long cap = (long long)num_sms() * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
     prep_kernel<<<(int)blocks, 256, 0, st>>>(x, x_dtype, token_sorted, expert_sorted, nrows, w13_suh, H, xt_g,
-                                             xt_u);
+                                             xt_u, rsum);
     return cudaGetLastError();
 }
 
