@@ -124,44 +124,83 @@ __global__ void __launch_bounds__(256) ep_gather_kernel(PeerTable peers, int wor
     }
 }
 
-// thread = (own token t, 8 consecutive columns)
+// block = own token t (grid-stride). Threads j < k first resolve route j of the token: the owner's sorted
+// position (one peer load each, all routes at once) and the weight, into shared memory; then every thread
+// takes 8-column chunks of the row and issues the loads of all routes' 16-byte pieces before it adds
+// them up in route order (fp32, the same order for every chunk), so the pull costs two dependent NVLink
+// round trips per token rather than two per route.
+constexpr int kCombineRoutes = 32;   // routes resolved per shared-memory batch
 __global__ void __launch_bounds__(256) ep_combine_kernel(PeerTable peers, int world, int rank, int tcap, int k,
                                                          int e_loc, uint32_t stamp, size_t out_flags_off,
                                                          const int* ids, const float* w, int T, int H,
                                                          size_t route_pos_off, size_t y_off, float* out, int* status,
                                                          uint64_t limit_ns)
 {
+    __shared__ const __half* src[kCombineRoutes];
+    __shared__ float wts[kCombineRoutes];
     const uint32_t* flags =
         reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(peers.base[rank]) + out_flags_off);
     const bool ok = block_wait_stamps(flags, world, stamp, status, limit_ns);
     const int chunks = H / 8;
-    const long long n = (long long)T * chunks;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-        const int t = (int)(i / chunks), c = (int)(i % chunks) * 8;
-        float acc[8];
+    for (int t = blockIdx.x; t < T; t += gridDim.x) {
+        // this thread's chunks of the row: c = threadIdx.x + 256 * i (at most 4 for H <= 8192)
+        float acc[4][8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] = 0.0f;
-        for (int j = 0; ok && j < k; ++j) {
-            const int e = ids[t * k + j];
-            if (e < 0) continue;
-            const int d = e / e_loc;
-            if (d >= world) continue;
-            const uint8_t* b = static_cast<const uint8_t*>(peers.base[d]);
-            const int pos = __ldcg(reinterpret_cast<const int*>(b + route_pos_off) + ((size_t)rank * tcap + t) * k + j);
-            if (pos < 0) continue;
-            const float wt = w[t * k + j];
-            const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(b + y_off) + (size_t)pos * H + c);
-            const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const __half2 h = u32_as_half2(v[q]);
-                acc[2 * q] = __fmaf_rn(wt, __low2float(h), acc[2 * q]);
-                acc[2 * q + 1] = __fmaf_rn(wt, __high2float(h), acc[2 * q + 1]);
+            for (int q = 0; q < 8; ++q) acc[i][q] = 0.0f;
+        for (int j0 = 0; ok && j0 < k; j0 += kCombineRoutes) {
+            const int nj = min(kCombineRoutes, k - j0);
+            if ((int)threadIdx.x < nj) {
+                const int j = j0 + threadIdx.x;
+                const int e = ids[t * k + j];
+                const __half* sp = nullptr;
+                float wt = 0.0f;
+                if (e >= 0 && e / e_loc < world) {
+                    const uint8_t* b = static_cast<const uint8_t*>(peers.base[e / e_loc]);
+                    const int pos = __ldcg(reinterpret_cast<const int*>(b + route_pos_off) + ((size_t)rank * tcap + t) * k + j);
+                    if (pos >= 0) {
+                        sp = reinterpret_cast<const __half*>(b + y_off) + (size_t)pos * H;
+                        wt = w[t * k + j];
+                    }
+                }
+                src[threadIdx.x] = sp;
+                wts[threadIdx.x] = wt;
             }
+            __syncthreads();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int c = (int)threadIdx.x + 256 * i;
+                if (c >= chunks) break;
+                for (int jb = 0; jb < nj; jb += 8) {
+                    uint4 u[8];
+#pragma unroll
+                    for (int r = 0; r < 8; ++r)
+                        if (jb + r < nj && src[jb + r]) u[r] = *reinterpret_cast<const uint4*>(src[jb + r] + (size_t)c * 8);
+#pragma unroll
+                    for (int r = 0; r < 8; ++r) {
+                        if (jb + r >= nj || !src[jb + r]) continue;
+                        const float wt = wts[jb + r];
+                        const uint32_t v[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const __half2 h = u32_as_half2(v[q]);
+                            acc[i][2 * q] = __fmaf_rn(wt, __low2float(h), acc[i][2 * q]);
+                            acc[i][2 * q + 1] = __fmaf_rn(wt, __high2float(h), acc[i][2 * q + 1]);
+                        }
+                    }
+                }
+            }
+            __syncthreads();
         }
-        float* o = out + (size_t)t * H + c;
-        *reinterpret_cast<float4*>(o) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        *reinterpret_cast<float4*>(o + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int c = (int)threadIdx.x + 256 * i;
+            if (c >= chunks) break;
+            float* o = out + (size_t)t * H + (size_t)c * 8;
+            *reinterpret_cast<float4*>(o) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+            *reinterpret_cast<float4*>(o + 4) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+        }
     }
 }
 
@@ -201,7 +240,8 @@ cudaError_t launch_ep_combine(const PeerTable& peers, int world, int rank, int t
                               size_t out_flags_off, const int* ids, const float* w, int T, int H, size_t route_pos_off,
                               size_t y_off, float* out, int* status, uint64_t limit_ns, cudaStream_t st)
 {
-    ep_combine_kernel<<<grid_for((long long)T * (H / 8), 256, 16), 256, 0, st>>>(
+    if (H > 8 * 256 * 4) return cudaErrorInvalidValue;   // the combine's 4 chunks of 8 columns per thread
+    ep_combine_kernel<<<grid_for(T, 1, 8), 256, 0, st>>>(
         peers, world, rank, tcap, k, e_loc, stamp, out_flags_off, ids, w, T, H, route_pos_off, y_off, out, status,
         limit_ns);
     return cudaGetLastError();

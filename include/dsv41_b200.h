@@ -205,7 +205,7 @@ int dsv41_moe_forward_logits(const dsv41_moe_layer* layer, const void* x, int32_
  * plain peer loads; step stamps in the shared buffers order the ranks (bounded waits, status 1
  * on expiry -> dsv41_ep_peer_read_status). Every rank must call it once per step with the same
  * `step` sequence (0, 1, 2, ...), topk and tokens_cap. The buffers alternate by step parity, so a
- * CUDA graph of one step replays only for steps of the same parity.
+ * CUDA graph of one step replays only for steps of the same parity. Hidden size up to 8192.
  * ------------------------------------------------------------------------------------------ */
 #define DSV41_MAX_PEERS 8
 #define DSV41_IPC_HANDLE_BYTES 64
