@@ -242,18 +242,18 @@ __device__ __forceinline__ void out_block128(float (&v)[128], const __half* svh)
 }
 
 // gate/up epilogue of one row and one 128-feature block (accumulators at TMEM columns tg / tu of this
-// thread's lane, sums of the affine weight codes times the inputs): g = KINV * acc_g + bias_g (bias =
-// KBIAS * the row's input sum), likewise u; v = H128(fp16(act(out_block(g), out_block(u))) * suh_d) *
+// thread's lane, sums of the affine weight codes times the inputs): g = KINV * acc_g + KBIAS * rsum[0]
+// (the row's gate input sum; NULL for rows past the pass), likewise u; v = H128(fp16(act(out_block(g),
+// out_block(u))) * suh_d) *
 // HAD, the down-input row before its fp16 rounding. Intermediate blocks are parked in TMEM, 32 columns
 // at a time, so no more than 128 + 64 values are live in registers.
 __device__ __forceinline__ void gateup_epilogue(float (&v)[128], uint32_t tg, uint32_t tu, const __half* svg,
-                                                const __half* svu, const __half* sd, float limit, float bias_g,
-                                                float bias_u)
+                                                const __half* svu, const __half* sd, float limit, const float* rsum)
 {
 #pragma unroll 1
     for (int m = 0; m < 2; ++m) {
         const uint32_t col = m ? tu : tg;
-        const float bias = m ? bias_u : bias_g;
+        const float bias = rsum ? kKbias * rsum[m] : 0.0f;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             float t[32];
@@ -601,15 +601,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 if (MODE == 0) {
                     const uint32_t colg = (uint32_t)((mt * 2 + 0) * kBN), colu = (uint32_t)((mt * 2 + 1) * kBN);
                     const __half* svg = p.svh_a + (size_t)e * 2 * p.N + fb * kBN;
-                    const float2 rs = live ? *reinterpret_cast<const float2*>(p.rs + 2 * grow) : make_float2(0.f, 0.f);
                     gateup_epilogue(v, lane_addr + colg, lane_addr + colu, svg, svg + p.N,
-                                    p.suh_d + (size_t)e * p.N + fb * kBN, p.limit, kKbias * rs.x, kKbias * rs.y);
-                    if (live) {   // block sum of the stored down inputs (the down pass's affine form)
-                        float bs = 0.0f;
-#pragma unroll
-                        for (int i = 0; i < 128; ++i) bs += r16(v[i]);
-                        p.xs_out[grow * (p.N / kBN) + fb] = bs;
-                    }
+                                    p.suh_d + (size_t)e * p.N + fb * kBN, p.limit, live ? p.rs + 2 * grow : nullptr);
                 } else {
                     float xs = 0.0f;
                     if (live)
@@ -622,14 +615,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 if (live) {
                     // 256 B of the row as eight 32-byte stores (rows are 4-8 KB, blocks 256 B: 32-byte aligned)
                     __half* dst = p.out + (size_t)(row0 + row) * p.N + fb * kBN;
+                    float bs = 0.0f;   // gate/up: block sum of the stored down inputs (the down pass's affine form)
 #pragma unroll
                     for (int c16 = 0; c16 < 8; ++c16) {
                         uint32_t o[8];
 #pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            o[j] = half2_as_u32(__floats2half2_rn(v[c16 * 16 + 2 * j], v[c16 * 16 + 2 * j + 1]));
+                        for (int j = 0; j < 8; ++j) {
+                            const __half2 h = __floats2half2_rn(v[c16 * 16 + 2 * j], v[c16 * 16 + 2 * j + 1]);
+                            if (MODE == 0) bs += __low2float(h) + __high2float(h);
+                            o[j] = half2_as_u32(h);
+                        }
                         st_global_32B(dst + c16 * 16, o);
                     }
+                    if (MODE == 0) p.xs_out[grow * (p.N / kBN) + fb] = bs;
                 }
             }
             tc_fence_before();
