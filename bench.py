@@ -47,6 +47,7 @@ sys.path.insert(0, ROOT)
 E, H, I, TOPK = 384, 4096, 2048, 8
 LIMIT = 10.0
 METRIC = "MoE-layer tok/s (decode B=64, prefill 16k) @1/2/4/8 B200; % HBM/tensor peak"
+GEMV_PROFILE = "gemv_decode_T64.txt"   # ncu summary of the decode-GEMV at the headline workload
 TILE_BYTES_PER_MATRIX = (H // 16) * (I // 16) * 96          # 3,145,728
 EXPERT_BYTES = 3 * TILE_BYTES_PER_MATRIX + (2 * H + 2 * I + I + H) * 2   # 9,474,048 (3 weight matrices + suh/svh)
 
@@ -226,24 +227,28 @@ def stage_times(fn, K, W):
             for s, name in enumerate(_lib.STAGE_NAMES)}
 
 
-def gateup_bytes(ids, T):
-    """Algorithmic bytes of one gate/up decode-GEMV launch: distinct experts' gate+up trellis, their
-    w13_svh and w2_suh channel scales, the transformed gate/up rows read once, the down-input rows
-    written once."""
+# compressed bytes one routed expert streams through the decode-GEMV (gate, up, down trellis and the
+# w13_svh, w2_suh, w2_svh scales it reads; w13_suh is read by the row transform)
+GEMV_EXPERT_BYTES = 3 * TILE_BYTES_PER_MATRIX + (2 * I + I + H) * 2
+# activation bytes per routed row: xt_g, xt_u read; the down input written and read back; y written
+GEMV_ROW_BYTES = 2 * H * 2 + I * 2 + I * 2 + H * 2
+
+
+def gemv_bytes(ids, T):
+    """Algorithmic bytes of one decode-GEMV launch (gate/up and down passes in one kernel): every distinct
+    routed expert's words and scales once, and each routed row's activations."""
     import numpy as np
     d = len(np.unique(ids))
-    rows = T * TOPK
-    return d * (2 * TILE_BYTES_PER_MATRIX + 2 * I * 2 + I * 2) + rows * 2 * H * 2 + rows * I * 2, d
+    return d * GEMV_EXPERT_BYTES + T * TOPK * GEMV_ROW_BYTES, d
 
 
-def gateup_bytes_ep(ids_all, lo, hi):
-    """gateup_bytes for the local forward of the rank owning experts [lo, hi) under expert
-    parallelism: distinct routed experts in its range, and the (token, rank) rows it receives."""
+def gemv_bytes_ep(ids_all, lo, hi):
+    """gemv_bytes for the local forward of the rank owning experts [lo, hi) under expert parallelism:
+    the distinct routed experts in its range and the routes it serves, over all ranks' tokens."""
     import numpy as np
     cat = np.concatenate([i.reshape(-1) for i in ids_all])
-    d = len(np.unique(cat[(cat >= lo) & (cat < hi)]))
-    rows = sum(int(((i >= lo) & (i < hi)).any(axis=1).sum()) for i in ids_all)
-    return d * (2 * TILE_BYTES_PER_MATRIX + 2 * I * 2 + I * 2) + rows * 2 * H * 2 + rows * I * 2, d
+    mine = cat[(cat >= lo) & (cat < hi)]
+    return len(np.unique(mine)) * GEMV_EXPERT_BYTES + mine.size * GEMV_ROW_BYTES, len(np.unique(mine))
 
 
 def layer_bytes(ids, T):
@@ -253,10 +258,10 @@ def layer_bytes(ids, T):
 
 
 def traffic_ratio_from_profile():
-    """DRAM bytes / algorithmic bytes of the gate/up GEMV launch captured with ncu (committed summary),
-    or None. Traffic per launch of this run = ratio x its algorithmic bytes per launch (the capture is
-    the same kernel and shape; the bytes scale with the distinct experts a batch routes to)."""
-    p = os.path.join(ROOT, "profiles", "gemv_gateup_decode_T64.txt")
+    """DRAM bytes / algorithmic bytes of the decode-GEMV launch captured with ncu (committed summary), or
+    None. Traffic per launch of this run = ratio x its algorithmic bytes per launch (the capture is the
+    same kernel and shape; the bytes scale with the distinct experts a batch routes to)."""
+    p = os.path.join(ROOT, "profiles", GEMV_PROFILE)
     if not os.path.exists(p):
         return None
     for line in open(p):
@@ -483,8 +488,9 @@ def stack_measure(a, kind, world, rank, dev, dist_on, hbm):
     # routes each rank serves and the gate/up decode-GEMV bytes of this rank's local forwards
     if kind == "ep40":
         all_ids = [[route_np(r, l)[0] for r in range(world)] for l in range(n_layers)]
-        gu = [gateup_bytes_ep(all_ids[l], lo, hi)[0] for l in range(n_layers)]
-        gemv_frac = statistics.mean(gu) / (st["gemv_gateup"] / 1e3) / 1e9 / hbm if st["gemv_gateup"] > 0 else None
+        gu = [gemv_bytes_ep(all_ids[l], lo, hi)[0] for l in range(n_layers)]
+        gemv_ms = st["gemv"] + st["gemv_down"]
+        gemv_frac = statistics.mean(gu) / (gemv_ms / 1e3) / 1e9 / hbm if gemv_ms > 0 else None
     else:
         gemv_frac = None
     if peer is not None:
@@ -534,7 +540,7 @@ def stack_measure(a, kind, world, rank, dev, dist_on, hbm):
                    "local_moe_ms_per_step": [round(float(v[2]), 3) for v in allv],
                    "a2a_and_dispatch_share": round(max(0.0, 1.0 - max(float(v[2]) for v in allv) / (ms / steps)), 4)}}
     if gemv_frac is not None:
-        line["ep"]["gemv_gateup_hbm_frac_rank0_layers"] = round(gemv_frac, 4)
+        line["ep"]["gemv_hbm_frac_rank0_layers"] = round(gemv_frac, 4)
     del layers, eps, routes
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
@@ -631,7 +637,7 @@ def main():
     # dominant kernel: per-stage events over the same steps
     st = stage_times(step, a.steps, 2)
     if world == 1:
-        gb = [gateup_bytes(ids, T) for _, ids, _ in host_batches]
+        gb = [gemv_bytes(ids, T) for _, ids, _ in host_batches]
         lb = [layer_bytes(ids, T) for _, ids, _ in host_batches]
     else:
         # what this rank's local forward streams: the distinct experts of [lo, hi) routed by any rank's
@@ -639,7 +645,7 @@ def main():
         gb, lb = [], []
         for b in range(a.batches):
             ids_all = [all_batches[r][b][1] for r in range(world)]
-            gb.append(gateup_bytes_ep(ids_all, lo, hi))
+            gb.append(gemv_bytes_ep(ids_all, lo, hi))
             rows = sum(int(((i >= lo) & (i < hi)).any(axis=1).sum()) for i in ids_all)
             lb.append(gb[-1][1] * EXPERT_BYTES + rows * H * 6 + rows * TOPK * 12)
     if eps is not None:
@@ -647,7 +653,8 @@ def main():
             e.stats = {k: 0 for k in e.stats}
     bytes_gu = statistics.mean(b for b, _ in gb)
     distinct = statistics.mean(d for _, d in gb)
-    achieved = bytes_gu / (st["gemv_gateup"] / 1e3) / 1e9
+    gemv_ms = st["gemv"] + st["gemv_down"]   # one launch with split 1 (gemv_down is then empty)
+    achieved = bytes_gu / (gemv_ms / 1e3) / 1e9
     layer_gbs = statistics.mean(lb) / (ms / a.steps / 1e3) / 1e9
     ratio = traffic_ratio_from_profile() if world == 1 else None  # the committed capture is the N=1 workload
     traffic = round(ratio * bytes_gu) if ratio else None
@@ -686,13 +693,13 @@ def main():
                    "parallelism": (f"expert parallel over {world} GPUs ({e_loc} experts each, {T} tokens per GPU), "
                                    "NCCL all-to-all dispatch/combine") if world > 1 else "single GPU",
                    "fat_threshold": fat},
-        "roofline": {"bound": "hbm", "kernel": "exl3_gemv_kernel<0> (decode-GEMV gate/up + act + down-input)",
+        "roofline": {"bound": "hbm", "kernel": "exl3_gemv_kernel (decode-GEMV: gate/up + SwiGLU + down, one launch)",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                     "traffic": traffic, "traffic_source": "profiles/gemv_gateup_decode_T64.txt DRAM/algorithmic "
+                     "traffic": traffic, "traffic_source": f"profiles/{GEMV_PROFILE} DRAM/algorithmic "
                      f"ratio {ratio} x bytes_per_launch" if ratio else None,
                      "peak_source": f"{peak_src} hbm_gbs (copy bandwidth)",
                      "bytes_per_launch": round(bytes_gu), "distinct_experts_per_step": round(distinct, 1),
-                     "avg_launch_ms": round(st["gemv_gateup"], 5)},
+                     "avg_launch_ms": round(gemv_ms, 5)},
         "layer_hbm": {"achieved_gbs": round(layer_gbs, 1), "frac": round(layer_gbs / hbm, 4),
                       "bytes_per_step": round(statistics.mean(lb))},
         "stage_ms": {k: round(v, 5) for k, v in st.items()},
@@ -761,10 +768,10 @@ def main():
             sms = time_steps(sstep, n, 5, dist_on)
             sst = stage_times(sstep, 64, 2)
             lbs = statistics.mean(layer_bytes(ids, Ts) for _, ids, _ in hbs)
-            gbs = statistics.mean(gateup_bytes(ids, Ts)[0] for _, ids, _ in hbs)
+            gbs = statistics.mean(gemv_bytes(ids, Ts)[0] for _, ids, _ in hbs)
             sweep[str(Ts)] = {"tok_s": round(world * Ts * n / (sms / 1e3), 1), "ms_per_step": round(sms / n, 5),
                               "layer_hbm_frac": round(lbs / (sms / n / 1e3) / 1e9 / hbm, 4),
-                              "gemv_gateup_hbm_frac": round(gbs / (sst["gemv_gateup"] / 1e3) / 1e9 / hbm, 4)}
+                              "gemv_hbm_frac": round(gbs / ((sst["gemv"] + sst["gemv_down"]) / 1e3) / 1e9 / hbm, 4)}
         line["sweep"] = sweep
 
     if not a.no_prefill and world == 1:

@@ -31,7 +31,8 @@ ABI_VERSION = 2
 MAX_PEERS = 8
 IPC_HANDLE_BYTES = 64
 N_STAGES = 7
-STAGE_NAMES = ("permute", "prep", "gemv_gateup", "gemm_gateup", "gemv_down", "gemm_down", "combine")
+# "gemv": the decode-GEMV launch (gate/up and down together when split-K is 1; "gemv_down" is then empty)
+STAGE_NAMES = ("permute", "prep", "gemv", "gemm_gateup", "gemv_down", "gemm_down", "combine")
 
 
 class MoeLayer(C.Structure):

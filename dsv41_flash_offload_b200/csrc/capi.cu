@@ -125,7 +125,7 @@ static Layout make_layout(int T, int topk, int E, int H, int I, int split_req, i
     L.xt_d = take(R * I * 2);
     L.y = take(R * H * 2);
     L.partials = take(L.split > 1 ? (size_t)L.units_bound * 4096 * 4 : 16);
-    L.counters = take((size_t)(L.units_bound / L.split + 1) * 4);
+    L.counters = take((size_t)(L.units_bound / L.split + 1 + gemv_sched_ints(L.groups_bound)) * 4);
     L.gemm = take(fat >= 0 ? gemm_scratch_bytes(L.rows, E, H, I) : 16);
     L.r_ids = take(N * 8);   // router output of dsv41_moe_forward_logits
     L.r_w = take(N * 4);
@@ -319,8 +319,11 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
     // row bound, so small calls (e.g. decode with T * topk <= fat) launch no GEMM kernels at all
     const bool gemm_on = fat >= 0 && rows_bound > fat;
     cudaError_t err;
+    // the split-K arrival counters, then the GEMV launches' ticket and ready counters
+    const int n_split_counters = gemv_units_alloc(groups_bound, H, I, split) / split + 1;
+    int* sched = counters + n_split_counters;
     if (split > 1) {
-        const size_t n = (size_t)(gemv_units_alloc(groups_bound, H, I, split) / split + 1) * 4;
+        const size_t n = (size_t)(n_split_counters + gemv_sched_ints(groups_bound)) * 4;
         if ((err = cudaMemsetAsync(counters, 0, n, st)) != cudaSuccess) return err;
     }
     GemmArgs ga{};
@@ -356,21 +359,31 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
     gp.out = xt_d;
     gp.K = H;
     gp.N = I;
-    if ((err = launch_gemv(0, gp, gemv_units_bound(groups_bound, H, I, 0, split), st)) != cudaSuccess) return err;
-    timer_mark(st, 3);
-    if (gemm_on && (err = launch_gemm_gateup(ga, st)) != cudaSuccess) return err;
-    timer_mark(st, 4);
-    gp.tab_a = layer->down_ptrs;
-    gp.tab_b = nullptr;
-    gp.xa = xt_d;
-    gp.xb = nullptr;
-    gp.svh_a = static_cast<const __half*>(layer->w2_svh);
-    gp.suh_d = nullptr;
-    gp.out = y;
-    gp.K = I;
-    gp.N = H;
-    if ((err = launch_gemv(1, gp, gemv_units_bound(groups_bound, I, H, 1, split), st)) != cudaSuccess) return err;
-    timer_mark(st, 5);
+    GemvParams gd = gp;
+    gd.tab_a = layer->down_ptrs;
+    gd.tab_b = nullptr;
+    gd.xa = xt_d;
+    gd.xb = nullptr;
+    gd.svh_a = static_cast<const __half*>(layer->w2_svh);
+    gd.suh_d = nullptr;
+    gd.out = y;
+    gd.K = I;
+    gd.N = H;
+    if (split == 1) {
+        // both decode-GEMV passes in one launch (stage "gemv_gateup"; "gemv_down" stays empty)
+        if ((err = launch_gemv_passes(gp, gd, 0, 1, sched, groups_bound, true, st)) != cudaSuccess) return err;
+        timer_mark(st, 3);
+        if (gemm_on && (err = launch_gemm_gateup(ga, st)) != cudaSuccess) return err;
+        timer_mark(st, 4);
+        timer_mark(st, 5);
+    } else {
+        if ((err = launch_gemv_passes(gp, gd, 0, 0, sched, groups_bound, false, st)) != cudaSuccess) return err;
+        timer_mark(st, 3);
+        if (gemm_on && (err = launch_gemm_gateup(ga, st)) != cudaSuccess) return err;
+        timer_mark(st, 4);
+        if ((err = launch_gemv_passes(gp, gd, 1, 1, sched, groups_bound, false, st)) != cudaSuccess) return err;
+        timer_mark(st, 5);
+    }
     if (gemm_on && (err = launch_gemm_down(ga, st)) != cudaSuccess) return err;
     timer_mark(st, 6);
     return cudaSuccess;
@@ -781,7 +794,7 @@ static size_t expert_gemm_layout(int R, int n_experts, int H, int I, size_t* off
     offs[9] = take(n * I * 2);                // xt_d
     offs[10] = take(n * H * 2);               // y
     offs[11] = take(split > 1 ? (size_t)gemv_units_alloc(gb, H, I, split) * 4096 * 4 : 16);
-    offs[12] = take((size_t)(gemv_units_alloc(gb, H, I, split) / split + 1) * 4);
+    offs[12] = take((size_t)(gemv_units_alloc(gb, H, I, split) / split + 1 + gemv_sched_ints(gb)) * 4);
     offs[13] = take(gemm_scratch_bytes(R, n_experts, H, I));
     offs[14] = (size_t)split;
     offs[15] = (size_t)gb;

@@ -47,7 +47,10 @@ namespace dsv41 {
 // (two MMAs per tile) with exact weights 1.217 ms; the same with affine codes 1.177; weights as the A
 // operand, exact 1.122, affine 1.102 (kept). Not kept: byte sums on the tensor pipe (two int8 MMAs per
 // tile instead of 8 DP4A) 1.279; one tile per warp (16 consumer warps) 1.277; 3 CTAs/SM with 8-row
-// stages 1.147; 8-row stages x 4 1.176. Earlier: 16-row stages x 2 beat 8 x 4 and 1 or 3 CTAs/SM.
+// stages 1.147; 8-row stages x 4 1.176; an L2 prefetch of the trellis rows 4 or 8 stages ahead of the
+// ring 1.185 (and T=1 0.046 -> 0.061 ms). Earlier: 16-row stages x 2 beat 8 x 4 and 1 or 3 CTAs/SM.
+// The one-CTA form (KS = 2, 4 stages) takes T=1 from 0.0473 to 0.0463 ms: small calls are bound by the
+// same per-SM decode rate (128 units = 8 experts x 16 column blocks on 128 SMs).
 
 #ifndef DSV41_GEMV_AFFINE
 #define DSV41_GEMV_AFFINE 1
@@ -61,30 +64,42 @@ namespace dsv41 {
 #endif
 
 constexpr int kTilesPerWarp = DSV41_GEMV_TILES_PER_WARP;
-constexpr int kConsumerWarps = 16 / kTilesPerWarp;   // 16 n-tiles per staged k-row
-constexpr int kGemvThreads = (kConsumerWarps + 1) * 32;
+// KS = 1: 8 consumer warps cover the 16 n-tiles of each staged k-row, 2 CTAs per SM (the default).
+// KS = 2 (calls with fewer units than SMs, e.g. one-token decode): 16 consumer warps in one CTA per SM,
+// warp w decodes the tiles of warp w % 8 on the k-rows of parity w / 8, and the two partial sums are
+// added in shared memory in a fixed order -- twice the warps per unit without global partials.
+template <int KS>
+__host__ __device__ constexpr int consumer_warps() { return KS * 16 / kTilesPerWarp; }
+template <int KS>
+__host__ __device__ constexpr int gemv_threads() { return (consumer_warps<KS>() + 1) * 32; }
 constexpr int kStageRows = DSV41_GEMV_STAGE_ROWS;
-constexpr int kStages = DSV41_GEMV_STAGES;
+// ring stages: the 2-CTA form (KS = 1) fits two 16-row stages per CTA; the one-CTA form (KS = 2) four
+template <int KS>
+__host__ __device__ constexpr int gemv_stages() { return KS == 1 ? DSV41_GEMV_STAGES : 2 * DSV41_GEMV_STAGES; }
+
 template <int K>
 __host__ __device__ constexpr int row_bytes() { return 16 * TileFmt<K>::bytes; }   // 16 tiles of one k-row (1536 B at K = 3)
 constexpr int kXRowStride = kStageRows * 32 + 16;  // stage's k-tiles x 16 halves, + 16 B pad (ldmatrix banks)
 constexpr int kXMatBytes = 16 * kXRowStride;
 constexpr int kEpFloats = 4096;
 
-template <int K>
+template <int K, int ST>
 struct GemvSmem {
+    static constexpr int kStages = ST;
     uint8_t tr[kStages][kStageRows * row_bytes<K>()];
     uint8_t x[kStages][2][kXMatBytes];
     float ep[kEpFloats];
     uint64_t full[kStages];
     uint64_t empty[kStages];
+    int stage_unit[kStages];   // ticket of the unit a stage belongs to (-1: no more work)
+    int next_unit;             // consumers' shared decision of the next unit
     int abort_flag;
     int last_flag;
 };
 
 size_t gemv_smem_bytes(int bits)
 {
-    return bits == 2 ? sizeof(GemvSmem<2>) : bits == 4 ? sizeof(GemvSmem<4>) : sizeof(GemvSmem<3>);
+    return bits == 2 ? sizeof(GemvSmem<2, 2>) : bits == 4 ? sizeof(GemvSmem<4, 2>) : sizeof(GemvSmem<3, 2>);
 }
 int gemv_stage_rows() { return kStageRows; }
 
@@ -109,14 +124,15 @@ __device__ __forceinline__ void ldmatrix_x2(uint32_t (&a)[4], uint32_t addr)
 // block), then per tile the decoded A fragment {b0, b2, b1, b3} (decode_tile returns the lane's
 // weights in B-fragment register order: (k 2q.., n g), (k 2q+8.., n g), (k 2q.., n g+8), (k 2q+8..,
 // n g+8)) and one MMA per n8 block. The affine form adds the token sums from an all-ones A.
-template <int K, bool TWO>
+template <int K, bool TWO, int KS>
 __device__ __forceinline__ void gemv_stage(const uint32_t* trow, uint32_t xaddr, const LaneDec<K>& lw,
                                                    uint32_t k16, float (&acc)[kTilesPerWarp][2][4],
-                                                   float (&rs)[2][4])
+                                                   float (&rs)[2][4], int par)
 {
     constexpr int kTW = TileFmt<K>::words, kRowWords = row_bytes<K>() / 4;
 #pragma unroll
-    for (int r = 0; r < kStageRows; ++r) {
+    for (int r0 = 0; r0 < kStageRows; r0 += KS) {
+        const int r = r0 + par;
         uint32_t bx[4];
         if (TWO)
             ldmatrix_x4(bx, xaddr + r * 32);
@@ -143,21 +159,297 @@ __device__ __forceinline__ void gemv_stage(const uint32_t* trow, uint32_t xaddr,
     }
 }
 
-template <int MODE, int K>
-__global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv_kernel(const GemvParams p)
+// One decode-GEMV launch: pass 0 (gate/up) and/or pass 1 (down) of the same row groups. Units of pass
+// m: n_groups x (N_m / cols_m) x split_m. The producer warp of each CTA takes units from a global ticket
+// counter, in order, and hands each to its consumer warps through the ring (the unit's ticket rides in
+// the stage slot), so the units handed out are always being processed by running CTAs: a launch that
+// runs both passes takes every gate/up unit first, and the producer of a down unit of group g waits
+// (bounded) until all gate/up units of g have stored their rows (ready[g]) -- no dependence on which
+// CTAs are resident, and the down units fill the gate/up pass's last wave.
+struct GemvWork {
+    GemvParams p[2];
+    int first, last;   // passes run: first..last
+    int* tickets;      // [1] next unit (zero before the launch)
+    int* ready;        // [groups] finished gate/up units per group (zero; used when both passes run)
+};
+
+template <int MODE>
+__device__ __forceinline__ int gemv_pass_units(const GemvParams& p, int ng)
 {
-    extern __shared__ __align__(128) uint8_t smem_raw[];
-    GemvSmem<K>& S = *reinterpret_cast<GemvSmem<K>*>(smem_raw);
-    constexpr int kTB = TileFmt<K>::bytes, kTW = TileFmt<K>::words, kRowBytes = row_bytes<K>();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    return ng * (p.N / (MODE == 0 ? 128 : 256)) * p.split;
+}
+
+// bounded wait until *cnt >= need (acquire, gpu scope); false (status 1) on expiry or abort
+__device__ __forceinline__ bool wait_count(const int* cnt, int need, volatile int* abort_flag, int* status)
+{
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+        if (v >= need) return true;
+        if ((it & 15u) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                *abort_flag = 1;
+                if (status) atomicExch(status, kStatusWaitTimeout);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// producer side of one unit (ticket v): its stages' bulk copies into the ring
+template <int MODE, int K, int ST>
+__device__ __forceinline__ bool gemv_produce(const GemvParams& p, GemvSmem<K, ST>& S, int u, int v, uint32_t& it,
+                                             int lane, uint64_t pol_w, uint64_t pol_x, const int* ready,
+                                             int ready_need)
+{
+    constexpr int kTB = TileFmt<K>::bytes, kRowBytes = row_bytes<K>();
     constexpr int nmat = MODE == 0 ? 2 : 1;
     constexpr int cols = MODE == 0 ? 128 : 256;
-    const int ktiles = p.K / 16;
     const int n_cb = p.N / cols;
-    const int k_per_split = ktiles / p.split;
+    const int k_per_split = p.K / 16 / p.split;
     const int stages_per_unit = k_per_split / kStageRows;
-    const int n_units = (*p.n_groups) * n_cb * p.split;
     const int ntile_row = p.N / 16;
+    const int s = u % p.split, ucb = u / p.split, cb = ucb % n_cb, g = ucb / n_cb;
+    const int4 G = p.groups[g];
+    const int e = G.x, row0 = G.y, rows = G.z;
+    if (ready) {   // this down unit reads the group's gate/up outputs
+        int ok = 1;
+        if (lane == 0) ok = wait_count(ready + g, ready_need, &S.abort_flag, p.status) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) return false;
+        fence_proxy_async_global();   // the rows were written through the generic proxy
+    }
+    const uint8_t* ta = reinterpret_cast<const uint8_t*>(p.tab_a[e]);
+    const uint8_t* tb = MODE == 0 ? reinterpret_cast<const uint8_t*>(p.tab_b[e]) : nullptr;
+    for (int st = 0; st < stages_per_unit; ++st, ++it) {
+        const int stage = it % ST;
+        const uint32_t round = it / ST;
+        if (!mbar_wait_bounded(&S.empty[stage], (round & 1) ^ 1, &S.abort_flag, p.status)) return false;
+        const int kt0 = s * k_per_split + st * kStageRows;
+        if (lane == 0) {
+            S.stage_unit[stage] = v;
+            mbar_arrive_expect_tx(&S.full[stage], kStageRows * kRowBytes + nmat * rows * kStageRows * 32);
+        }
+        __syncwarp();
+        if (MODE == 0) {
+            if (lane < 2 * kStageRows) {
+                const int r = lane >> 1, which = lane & 1;
+                const uint8_t* src = (which ? tb : ta) + ((size_t)(kt0 + r) * ntile_row + cb * 8) * kTB;
+                bulk_g2s(S.tr[stage] + r * kRowBytes + which * 8 * kTB, src, 8 * kTB, &S.full[stage], pol_w);
+            }
+        } else {
+            if (lane < kStageRows) {
+                const uint8_t* src = ta + ((size_t)(kt0 + lane) * ntile_row + cb * 16) * kTB;
+                bulk_g2s(S.tr[stage] + lane * kRowBytes, src, kRowBytes, &S.full[stage], pol_w);
+            }
+        }
+        for (int c = lane; c < nmat * rows; c += 32) {
+            const int m = c / rows, j = c % rows;
+            const __half* src = (m ? p.xb : p.xa) + (size_t)(row0 + j) * p.K + kt0 * 16;
+            bulk_g2s(S.x[stage][m] + j * kXRowStride, src, kStageRows * 32, &S.full[stage], pol_x);
+        }
+    }
+    return true;
+}
+
+// consumer side of one unit: decode + MMAs over its stages, the ordered partial-sum merge, split-K
+// reduction and the epilogue; with `ready`, a gate/up unit counts itself done for its group
+template <int MODE, int K, int KS, int ST>
+__device__ __forceinline__ void gemv_consume(const GemvParams& p, GemvSmem<K, ST>& S, int u, uint32_t& it, int warp,
+                                             int lane, const LaneDec<K>& lw, int* ready)
+{
+    constexpr int kConsumerWarps = consumer_warps<KS>();
+    constexpr int kTW = TileFmt<K>::words;
+    constexpr int cols = MODE == 0 ? 128 : 256;
+    const int n_cb = p.N / cols;
+    const int stages_per_unit = p.K / 16 / p.split / kStageRows;
+    const uint32_t k16 = p.k16;
+    const int par = warp / 8;                              // k-row parity of this warp (KS = 2)
+    const int tile0 = (warp % 8) * kTilesPerWarp;          // first of this warp's adjacent n-tiles (0..15)
+    const int mat = MODE == 0 ? (tile0 >> 3) : 0;          // gate/up pass: tiles 0-7 gate, 8-15 up
+    // B fragments: matrices (tokens 0-7, k 0-7), (0-7, 8-15), (8-15, 0-7), (8-15, 8-15)
+    const uint32_t x_lane = ((lane & 7) + ((lane >> 4) & 1) * 8) * kXRowStride + ((lane >> 3) & 1) * 16;
+    const int ucb = u / p.split, cb = ucb % n_cb, g = ucb / n_cb;
+    const int4 G = p.groups[g];
+    const int e = G.x, row0 = G.y, rows = G.z;
+    float acc[kTilesPerWarp][2][4];
+#pragma unroll
+    for (int t = 0; t < kTilesPerWarp; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[t][h][q] = 0.f;
+    float rs[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};   // token sums (affine form)
+    const bool two = rows > 8;
+    for (int st = 0; st < stages_per_unit; ++st, ++it) {
+        const int stage = it % ST;
+        const uint32_t round = it / ST;
+        // a wait that runs out (or a CTA that already gave up) skips the stage's compute: the staged
+        // bytes may never have arrived. The warp still takes every barrier step below.
+        if (mbar_wait_bounded(&S.full[stage], round & 1, &S.abort_flag, p.status)) {
+            // this warp's tiles sit at byte offset tile * 32K of each staged 16-tile k-row
+            const uint32_t* trow = reinterpret_cast<const uint32_t*>(S.tr[stage]) + tile0 * kTW;
+            const uint32_t xaddr = smem_addr(S.x[stage][mat]) + x_lane;
+            if (two)
+                gemv_stage<K, true, KS>(trow, xaddr, lw, k16, acc, rs, par);
+            else
+                gemv_stage<K, false, KS>(trow, xaddr, lw, k16, acc, rs, par);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.empty[stage]);
+    }
+
+#if DSV41_GEMV_AFFINE
+    // sum_k w x = KINV * sum_k code x + KBIAS * sum_k x (per split: the partial sums add up the same)
+#pragma unroll
+    for (int t = 0; t < kTilesPerWarp; ++t)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[t][h][q] = fmaf(kKinv, acc[t][h][q], kKbias * rs[h][q]);
+#endif
+    // accumulators (feature g / g + 8 of the tile, tokens 8h + 2q, + 1) -> shared [mat][row][cols];
+    // with KS = 2 the odd-row warps add their partial sums to the even-row warps' (fixed order)
+#pragma unroll
+    for (int phase = 0; phase < KS; ++phase) {
+        if (par == phase) {
+#pragma unroll
+            for (int t = 0; t < kTilesPerWarp; ++t) {
+                const int tile = tile0 + t;
+                const int fcol = (MODE == 0 ? (tile & 7) : tile) * 16 + (lane >> 2);
+                float* ep = S.ep + (MODE == 0 ? mat * 16 * cols : 0);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    if (h == 1 && !two) break;
+                    const int tok = 8 * h + (lane & 3) * 2;
+                    float* e0 = ep + tok * cols + fcol;
+                    float* e1 = e0 + cols;
+                    if (phase == 0) {
+                        e0[0] = acc[t][h][0];
+                        e1[0] = acc[t][h][1];
+                        e0[8] = acc[t][h][2];
+                        e1[8] = acc[t][h][3];
+                    } else {
+                        e0[0] += acc[t][h][0];
+                        e1[0] += acc[t][h][1];
+                        e0[8] += acc[t][h][2];
+                        e1[8] += acc[t][h][3];
+                    }
+                }
+            }
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+    }
+
+    if (p.split > 1) {
+        float* slot = p.partials + (size_t)u * kEpFloats;
+        for (int i = threadIdx.x * 4; i < kEpFloats; i += kConsumerWarps * 32 * 4)
+            __stcg(reinterpret_cast<float4*>(slot + i), *reinterpret_cast<const float4*>(S.ep + i));
+        __threadfence();
+        named_bar_sync(1, kConsumerWarps * 32);
+        if (threadIdx.x == 0) {
+            const int old = atomicAdd(p.counters + ucb, 1);
+            S.last_flag = (old == p.split - 1);
+        }
+        named_bar_sync(1, kConsumerWarps * 32);
+        if (!S.last_flag) return;
+        __threadfence();
+        for (int i = threadIdx.x * 4; i < kEpFloats; i += kConsumerWarps * 32 * 4) {
+            float4 v = __ldcg(reinterpret_cast<const float4*>(p.partials + (size_t)ucb * p.split * kEpFloats + i));
+            for (int s2 = 1; s2 < p.split; ++s2) {
+                const float4 w = __ldcg(reinterpret_cast<const float4*>(
+                    p.partials + ((size_t)ucb * p.split + s2) * kEpFloats + i));
+                v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+            }
+            *reinterpret_cast<float4*>(S.ep + i) = v;
+        }
+        if (threadIdx.x == 0) p.counters[ucb] = 0;
+        named_bar_sync(1, kConsumerWarps * 32);
+    }
+
+    // epilogue: warp w transforms rows w, w + kConsumerWarps, ... of the group. Once this CTA has given
+    // up on a wait, its remaining rows are written as zeros (the status word says why).
+    const bool aborted = *reinterpret_cast<volatile int*>(&S.abort_flag) != 0;
+    for (int j = warp; j < rows; j += kConsumerWarps) {
+        if (aborted) {
+            for (int c = lane * 4; c < cols; c += 128)
+                *reinterpret_cast<uint2*>(p.out + (size_t)(row0 + j) * p.N + cb * cols + c) = make_uint2(0u, 0u);
+            continue;
+        }
+        if (MODE == 0) {
+            float gv[4], uv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                gv[q] = S.ep[j * 128 + lane * 4 + q];
+                uv[q] = S.ep[(16 + j) * 128 + lane * 4 + q];
+            }
+            const size_t sv = (size_t)e * 2 * p.N + cb * 128 + lane * 4;
+            out_block4(gv, p.svh_a + sv, lane);
+            out_block4(uv, p.svh_a + sv + p.N, lane);
+            const uint2 su = *reinterpret_cast<const uint2*>(p.suh_d + (size_t)e * p.N + cb * 128 + lane * 4);
+            const __half2 s01 = u32_as_half2(su.x), s23 = u32_as_half2(su.y);
+            const float sd[4] = {__low2float(s01), __high2float(s01), __low2float(s23), __high2float(s23)};
+            float v[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(r16(act_gu(gv[q], uv[q], p.limit)), sd[q]);
+            had128_warp(v, lane);
+            uint2 o;
+            o.x = half2_as_u32(__floats2half2_rn(__fmul_rn(v[0], kHad), __fmul_rn(v[1], kHad)));
+            o.y = half2_as_u32(__floats2half2_rn(__fmul_rn(v[2], kHad), __fmul_rn(v[3], kHad)));
+            *reinterpret_cast<uint2*>(p.out + (size_t)(row0 + j) * p.N + cb * 128 + lane * 4) = o;
+        } else {
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk) {
+                float y[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) y[q] = S.ep[j * 256 + blk * 128 + lane * 4 + q];
+                const size_t c = (size_t)cb * 256 + blk * 128 + lane * 4;
+                out_block4(y, p.svh_a + (size_t)e * p.N + c, lane);
+                uint2 o;
+                o.x = half2_as_u32(__floats2half2_rn(y[0], y[1]));
+                o.y = half2_as_u32(__floats2half2_rn(y[2], y[3]));
+                *reinterpret_cast<uint2*>(p.out + (size_t)(row0 + j) * p.N + c) = o;
+            }
+        }
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
+    if (MODE == 0 && ready && threadIdx.x == 0) {
+        // the group's rows of this column block are stored (every consumer warp passed the barrier):
+        // publish them to the down units' producers (bulk copies, the async proxy)
+        fence_proxy_async_global();
+        __threadfence();
+        atomicAdd(ready + g, 1);
+    }
+}
+
+template <int K, int KS>
+__global__ void __launch_bounds__(gemv_threads<KS>(), KS == 1 ? DSV41_GEMV_MIN_BLOCKS : 1)
+    exl3_gemv_kernel(const __grid_constant__ GemvWork w)
+{
+    constexpr int kConsumerWarps = consumer_warps<KS>();
+    constexpr int kStages = gemv_stages<KS>();
+    using Smem = GemvSmem<K, kStages>;
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    Smem& S = *reinterpret_cast<Smem*>(smem_raw);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ng = *w.p[w.first].n_groups;
+    const int u0 = w.first == 0 ? gemv_pass_units<0>(w.p[0], ng) : gemv_pass_units<1>(w.p[1], ng);
+    const int total = u0 + (w.last > w.first ? gemv_pass_units<1>(w.p[1], ng) : 0);
+    const bool fused = w.last > w.first;
+    // ticket v -> pass and unit within the pass
+    auto which = [&](int v, int& mode, int& u) {
+        if (v < u0) {
+            mode = w.first;
+            u = v;
+        } else {
+            mode = 1;
+            u = v - u0;
+        }
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -175,41 +467,27 @@ __global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv
         const uint64_t pol_x = l2_policy_evict_last();
         uint32_t it = 0;
         bool ok = true;
-        for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
-            const int s = u % p.split, ucb = u / p.split, cb = ucb % n_cb, g = ucb / n_cb;
-            const int4 G = p.groups[g];
-            const int e = G.x, row0 = G.y, rows = G.z;
-            const uint8_t* ta = reinterpret_cast<const uint8_t*>(p.tab_a[e]);
-            const uint8_t* tb = MODE == 0 ? reinterpret_cast<const uint8_t*>(p.tab_b[e]) : nullptr;
-            for (int st = 0; st < stages_per_unit; ++st, ++it) {
+        while (ok) {
+            int v = 0;
+            if (lane == 0) v = atomicAdd(w.tickets, 1);
+            v = __shfl_sync(0xffffffffu, v, 0);
+            if (v >= total) {
+                // end of the work: the next ring stage carries ticket -1
                 const int stage = it % kStages;
-                const uint32_t round = it / kStages;
-                if (!mbar_wait_bounded(&S.empty[stage], (round & 1) ^ 1, &S.abort_flag, p.status)) {
-                    ok = false;
-                    break;
+                ok = mbar_wait_bounded(&S.empty[stage], ((it / kStages) & 1) ^ 1, &S.abort_flag, w.p[w.first].status);
+                if (ok && lane == 0) {
+                    S.stage_unit[stage] = -1;
+                    mbar_arrive(&S.full[stage]);
                 }
-                const int kt0 = s * k_per_split + st * kStageRows;
-                if (lane == 0)
-                    mbar_arrive_expect_tx(&S.full[stage], kStageRows * kRowBytes + nmat * rows * kStageRows * 32);
-                __syncwarp();
-                if (MODE == 0) {
-                    if (lane < 2 * kStageRows) {
-                        const int r = lane >> 1, which = lane & 1;
-                        const uint8_t* src = (which ? tb : ta) + ((size_t)(kt0 + r) * ntile_row + cb * 8) * kTB;
-                        bulk_g2s(S.tr[stage] + r * kRowBytes + which * 8 * kTB, src, 8 * kTB, &S.full[stage], pol_w);
-                    }
-                } else {
-                    if (lane < kStageRows) {
-                        const uint8_t* src = ta + ((size_t)(kt0 + lane) * ntile_row + cb * 16) * kTB;
-                        bulk_g2s(S.tr[stage] + lane * kRowBytes, src, kRowBytes, &S.full[stage], pol_w);
-                    }
-                }
-                for (int c = lane; c < nmat * rows; c += 32) {
-                    const int m = c / rows, j = c % rows;
-                    const __half* src = (m ? p.xb : p.xa) + (size_t)(row0 + j) * p.K + kt0 * 16;
-                    bulk_g2s(S.x[stage][m] + j * kXRowStride, src, kStageRows * 32, &S.full[stage], pol_x);
-                }
+                break;
             }
+            int mode, u;
+            which(v, mode, u);
+            if (mode == 0)
+                ok = gemv_produce<0, K, kStages>(w.p[0], S, u, v, it, lane, pol_w, pol_x, nullptr, 0);
+            else
+                ok = gemv_produce<1, K, kStages>(w.p[1], S, u, v, it, lane, pol_w, pol_x, fused ? w.ready : nullptr,
+                                                 w.p[0].N / 128 * w.p[0].split);
         }
         if (!ok && lane == 0) {
             // drain: do not leave the CTA while copies into its shared memory are in flight
@@ -225,143 +503,23 @@ __global__ void __launch_bounds__(kGemvThreads, DSV41_GEMV_MIN_BLOCKS) exl3_gemv
 
     // ------------------------------ consumer warps ------------------------------
     const LaneDec<K> lw = lane_dec_setup<K>(lane);
-    const uint32_t k16 = p.k16;
-    const int tile0 = warp * kTilesPerWarp;       // first of this warp's adjacent n-tiles (0..15)
-    const int mat = MODE == 0 ? (tile0 >> 3) : 0;  // gate/up pass: tiles 0-7 gate, 8-15 up
-    // B fragments: matrices (tokens 0-7, k 0-7), (0-7, 8-15), (8-15, 0-7), (8-15, 8-15)
-    const uint32_t x_lane = ((lane & 7) + ((lane >> 4) & 1) * 8) * kXRowStride + ((lane >> 3) & 1) * 16;
     uint32_t it = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-        const int ucb = u / p.split, cb = ucb % n_cb, g = ucb / n_cb;
-        const int4 G = p.groups[g];
-        const int e = G.x, row0 = G.y, rows = G.z;
-        float acc[kTilesPerWarp][2][4];
-#pragma unroll
-        for (int t = 0; t < kTilesPerWarp; ++t)
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-#pragma unroll
-                for (int q = 0; q < 4; ++q) acc[t][h][q] = 0.f;
-        float rs[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};   // token sums (affine form)
-        const bool two = rows > 8;
-        for (int st = 0; st < stages_per_unit; ++st, ++it) {
-            const int stage = it % kStages;
-            const uint32_t round = it / kStages;
-            // a wait that runs out (or a CTA that already gave up) skips the stage's compute: the
-            // staged bytes may never have arrived. The warp still takes every barrier step below.
-            if (mbar_wait_bounded(&S.full[stage], round & 1, &S.abort_flag, p.status)) {
-                // this warp's tiles sit at byte offset tile * 32K of each staged 16-tile k-row
-                const uint32_t* trow = reinterpret_cast<const uint32_t*>(S.tr[stage]) + tile0 * kTW;
-                const uint32_t xaddr = smem_addr(S.x[stage][mat]) + x_lane;
-                if (two)
-                    gemv_stage<K, true>(trow, xaddr, lw, k16, acc, rs);
-                else
-                    gemv_stage<K, false>(trow, xaddr, lw, k16, acc, rs);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S.empty[stage]);
-        }
-
-#if DSV41_GEMV_AFFINE
-        // sum_k w x = KINV * sum_k code x + KBIAS * sum_k x (per split: the partial sums add up the same)
-#pragma unroll
-        for (int t = 0; t < kTilesPerWarp; ++t)
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-#pragma unroll
-                for (int q = 0; q < 4; ++q) acc[t][h][q] = fmaf(kKinv, acc[t][h][q], kKbias * rs[h][q]);
-#endif
-        // accumulators (feature g / g + 8 of the tile, tokens 8h + 2q, + 1) -> shared [mat][row][cols]
-#pragma unroll
-        for (int t = 0; t < kTilesPerWarp; ++t) {
-            const int tile = tile0 + t;
-            const int fcol = (MODE == 0 ? (tile & 7) : tile) * 16 + (lane >> 2);
-            float* ep = S.ep + (MODE == 0 ? mat * 16 * cols : 0);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                if (h == 1 && !two) break;
-                const int tok = 8 * h + (lane & 3) * 2;
-                ep[tok * cols + fcol] = acc[t][h][0];
-                ep[(tok + 1) * cols + fcol] = acc[t][h][1];
-                ep[tok * cols + fcol + 8] = acc[t][h][2];
-                ep[(tok + 1) * cols + fcol + 8] = acc[t][h][3];
-            }
-        }
+    for (;;) {
+        // the unit of the next stage, decided once for all consumer warps: thread 0 reads it (or -1 once
+        // the CTA has given up, including on a wait of the producer) between two consumer barriers
+        const int stage = it % kStages;
+        mbar_wait_bounded(&S.full[stage], (it / kStages) & 1, &S.abort_flag, w.p[w.first].status);
         named_bar_sync(1, kConsumerWarps * 32);
-
-        if (p.split > 1) {
-            float* slot = p.partials + (size_t)u * kEpFloats;
-            for (int i = threadIdx.x * 4; i < kEpFloats; i += kConsumerWarps * 32 * 4)
-                __stcg(reinterpret_cast<float4*>(slot + i), *reinterpret_cast<const float4*>(S.ep + i));
-            __threadfence();
-            named_bar_sync(1, kConsumerWarps * 32);
-            if (threadIdx.x == 0) {
-                const int old = atomicAdd(p.counters + ucb, 1);
-                S.last_flag = (old == p.split - 1);
-            }
-            named_bar_sync(1, kConsumerWarps * 32);
-            if (!S.last_flag) continue;
-            __threadfence();
-            for (int i = threadIdx.x * 4; i < kEpFloats; i += kConsumerWarps * 32 * 4) {
-                float4 v = __ldcg(reinterpret_cast<const float4*>(p.partials + (size_t)ucb * p.split * kEpFloats + i));
-                for (int s2 = 1; s2 < p.split; ++s2) {
-                    const float4 w = __ldcg(reinterpret_cast<const float4*>(
-                        p.partials + ((size_t)ucb * p.split + s2) * kEpFloats + i));
-                    v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
-                }
-                *reinterpret_cast<float4*>(S.ep + i) = v;
-            }
-            if (threadIdx.x == 0) p.counters[ucb] = 0;
-            named_bar_sync(1, kConsumerWarps * 32);
-        }
-
-        // epilogue: warp w transforms rows w, w + kConsumerWarps, ... of the group. Once this CTA has
-        // given up on a wait, its remaining rows are written as zeros (the status word says why).
-        const bool aborted = *reinterpret_cast<volatile int*>(&S.abort_flag) != 0;
-        for (int j = warp; j < rows; j += kConsumerWarps) {
-            if (aborted) {
-                const int n = MODE == 0 ? 128 : 256;
-                for (int c = lane * 4; c < n; c += 128)
-                    *reinterpret_cast<uint2*>(p.out + (size_t)(row0 + j) * p.N + cb * n + c) = make_uint2(0u, 0u);
-                continue;
-            }
-            if (MODE == 0) {
-                float gv[4], uv[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    gv[q] = S.ep[j * 128 + lane * 4 + q];
-                    uv[q] = S.ep[(16 + j) * 128 + lane * 4 + q];
-                }
-                const size_t sv = (size_t)e * 2 * p.N + cb * 128 + lane * 4;
-                out_block4(gv, p.svh_a + sv, lane);
-                out_block4(uv, p.svh_a + sv + p.N, lane);
-                const uint2 su = *reinterpret_cast<const uint2*>(p.suh_d + (size_t)e * p.N + cb * 128 + lane * 4);
-                const __half2 s01 = u32_as_half2(su.x), s23 = u32_as_half2(su.y);
-                const float sd[4] = {__low2float(s01), __high2float(s01), __low2float(s23), __high2float(s23)};
-                float v[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) v[q] = __fmul_rn(r16(act_gu(gv[q], uv[q], p.limit)), sd[q]);
-                had128_warp(v, lane);
-                uint2 o;
-                o.x = half2_as_u32(__floats2half2_rn(__fmul_rn(v[0], kHad), __fmul_rn(v[1], kHad)));
-                o.y = half2_as_u32(__floats2half2_rn(__fmul_rn(v[2], kHad), __fmul_rn(v[3], kHad)));
-                *reinterpret_cast<uint2*>(p.out + (size_t)(row0 + j) * p.N + cb * 128 + lane * 4) = o;
-            } else {
-#pragma unroll
-                for (int blk = 0; blk < 2; ++blk) {
-                    float y[4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) y[q] = S.ep[j * 256 + blk * 128 + lane * 4 + q];
-                    const size_t c = (size_t)cb * 256 + blk * 128 + lane * 4;
-                    out_block4(y, p.svh_a + (size_t)e * p.N + c, lane);
-                    uint2 o;
-                    o.x = half2_as_u32(__floats2half2_rn(y[0], y[1]));
-                    o.y = half2_as_u32(__floats2half2_rn(y[2], y[3]));
-                    *reinterpret_cast<uint2*>(p.out + (size_t)(row0 + j) * p.N + c) = o;
-                }
-            }
-        }
+        if (threadIdx.x == 0) S.next_unit = *reinterpret_cast<volatile int*>(&S.abort_flag) ? -1 : S.stage_unit[stage];
         named_bar_sync(1, kConsumerWarps * 32);
+        const int v = S.next_unit;
+        if (v < 0) break;
+        int mode, u;
+        which(v, mode, u);
+        if (mode == 0)
+            gemv_consume<0, K, KS, kStages>(w.p[0], S, u, it, warp, lane, lw, fused ? w.ready : nullptr);
+        else
+            gemv_consume<1, K, KS, kStages>(w.p[1], S, u, it, warp, lane, lw, nullptr);
     }
 }
 
@@ -378,25 +536,52 @@ int gemv_units_alloc(int groups_bound, int H, int I, int split)
     return groups_bound * cb * split;
 }
 
-template <int MODE, int K>
-static cudaError_t launch_gemv_k(const GemvParams& p, int units_bound, cudaStream_t st)
+template <int K, int KS>
+static cudaError_t launch_work_k(const GemvWork& w, int units_bound, cudaStream_t st)
 {
-    const size_t smem = sizeof(GemvSmem<K>);
-    cudaError_t err = cudaFuncSetAttribute((const void*)exl3_gemv_kernel<MODE, K>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const size_t smem = sizeof(GemvSmem<K, gemv_stages<KS>()>);
+    cudaError_t err =
+        cudaFuncSetAttribute((const void*)exl3_gemv_kernel<K, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (err != cudaSuccess) return err;
-    int grid = DSV41_GEMV_MIN_BLOCKS * num_sms();
+    int grid = (KS == 1 ? DSV41_GEMV_MIN_BLOCKS : 1) * num_sms();
     if (units_bound < grid) grid = units_bound;
     if (grid < 1) grid = 1;
-    exl3_gemv_kernel<MODE, K><<<grid, kGemvThreads, smem, st>>>(p);
+    exl3_gemv_kernel<K, KS><<<grid, gemv_threads<KS>(), smem, st>>>(w);
     return cudaGetLastError();
 }
 
-cudaError_t launch_gemv(int mode, const GemvParams& p, int units_bound, cudaStream_t st)
+// calls whose passes each fit in one CTA per SM run the 16-warp form (twice the warps per unit)
+template <int K>
+static cudaError_t launch_work(const GemvWork& w, int pass_bound, int units_bound, cudaStream_t st)
 {
-    if (p.bits == 2) return mode == 0 ? launch_gemv_k<0, 2>(p, units_bound, st) : launch_gemv_k<1, 2>(p, units_bound, st);
-    if (p.bits == 4) return mode == 0 ? launch_gemv_k<0, 4>(p, units_bound, st) : launch_gemv_k<1, 4>(p, units_bound, st);
-    return mode == 0 ? launch_gemv_k<0, 3>(p, units_bound, st) : launch_gemv_k<1, 3>(p, units_bound, st);
+    if (pass_bound <= num_sms()) return launch_work_k<K, 2>(w, units_bound, st);
+    return launch_work_k<K, 1>(w, units_bound, st);
+}
+
+int gemv_sched_ints(int groups_bound) { return groups_bound + 2; }
+
+cudaError_t launch_gemv_passes(const GemvParams& gateup, const GemvParams& down, int first, int last, int* sched,
+                               int groups_bound, bool clear, cudaStream_t st)
+{
+    if (clear) {
+        const cudaError_t err = cudaMemsetAsync(sched, 0, (size_t)gemv_sched_ints(groups_bound) * 4, st);
+        if (err != cudaSuccess) return err;
+    }
+    GemvWork w{};
+    w.p[0] = gateup;
+    w.p[1] = down;
+    w.first = first;
+    w.last = last;
+    w.tickets = sched + first;   // one ticket counter per pass launch
+    w.ready = sched + 2;
+    const int b0 = gemv_units_bound(groups_bound, gateup.K, gateup.N, 0, gateup.split);
+    const int b1 = gemv_units_bound(groups_bound, down.K, down.N, 1, down.split);
+    const int pass_bound = first == 0 && last == 0 ? b0 : first == 1 ? b1 : (b0 > b1 ? b0 : b1);
+    const int units_bound = (first == 0 ? b0 : 0) + (last == 1 ? b1 : 0);
+    const int bits = first == 0 ? gateup.bits : down.bits;
+    if (bits == 2) return launch_work<2>(w, pass_bound, units_bound, st);
+    if (bits == 4) return launch_work<4>(w, pass_bound, units_bound, st);
+    return launch_work<3>(w, pass_bound, units_bound, st);
 }
 
 }  // namespace dsv41

@@ -103,7 +103,13 @@ int gemv_units_bound(int groups_bound, int K, int N, int mode, int split);
 int gemv_units_alloc(int groups_bound, int H, int I, int split);
 size_t gemv_smem_bytes(int bits);
 int gemv_stage_rows();   // k-tile rows per pipeline stage: a K split must be a multiple of it
-cudaError_t launch_gemv(int mode, const GemvParams& p, int units_bound, cudaStream_t st);
+// Decode-GEMV passes first..last (0 = gate/up, 1 = down) of the same row groups in one launch; both
+// passes run together only with split 1 (the down units wait for their group's gate/up units).
+// sched: gemv_sched_ints(groups_bound) ints of workspace (ticket counters, per-group ready counters),
+// zeroed by the launch when `clear`.
+int gemv_sched_ints(int groups_bound);
+cudaError_t launch_gemv_passes(const GemvParams& gateup, const GemvParams& down, int first, int last, int* sched,
+                               int groups_bound, bool clear, cudaStream_t st);
 
 cudaError_t launch_combine(const __half* y, const int* route_pos, const float* w, int T, int topk,
                            int H, int accumulate, float* out, cudaStream_t st);

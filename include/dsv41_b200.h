@@ -235,7 +235,8 @@ int dsv41_ep_peer_read_status(const dsv41_ep_peer_group* group, const dsv41_moe_
  * it runs on). While enabled, dsv41_moe_forward records CUDA events at its stage boundaries for up
  * to DSV41_TIMING_MAX_CALLS calls (not under stream capture). dsv41_read_stage_times synchronises
  * them and writes DSV41_N_STAGES times in ms per recorded call, in the order permute, row prep,
- * gate/up GEMV, gate/up GEMM, down GEMV, down GEMM, combine; then it forgets them. */
+ * decode-GEMV (both passes, one launch, when split_k is 1), gate/up GEMM, down decode-GEMV (its own
+ * launch when split_k > 1, else empty), down GEMM, combine; then it forgets them. */
 #define DSV41_N_STAGES 7
 #define DSV41_TIMING_MAX_CALLS 256
 int dsv41_set_stage_timing(int32_t enable);
