@@ -56,7 +56,7 @@ namespace dsv41 {
 #define DSV41_GEMV_AFFINE 1
 #endif
 #ifndef DSV41_GEMV_IMAD_PACKS
-#define DSV41_GEMV_IMAD_PACKS 4       // of the 4 half2 code packs per lane and tile, how many on IMAD
+#define DSV41_GEMV_IMAD_PACKS 3       // of the 4 half2 code packs per lane and tile, how many on IMAD (measured 2: 1.577, 3: 1.556, 4: 1.576 ms GEMV at T=64)
 #endif
 
 #ifndef DSV41_GEMV_TILES_PER_WARP
