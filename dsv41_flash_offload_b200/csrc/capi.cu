@@ -173,9 +173,11 @@ static PermBuffers perm_buffers(void* ws, const Layout& L)
 constexpr size_t kCtrlInFlags = 0;     // uint32 in_flag[kMaxPeers]: step stamps written by peers
 constexpr size_t kCtrlOutFlags = 64;   // uint32 out_flag[kMaxPeers]
 constexpr size_t kCtrlStatus = 128;    // int status of the exchange waits
+constexpr size_t kCtrlOutDrop = 160;   // uint32 out_drop[kMaxPeers]: stamp of a step whose routes a peer dropped
+constexpr size_t kCtrlPubDone = 224;   // int: blocks of this rank's publish launch that finished
 
 struct PeerLayout {
-    size_t ctrl, x[2], ids[2], w[2], ids_loc[2], w_loc[2], ws[2], total;
+    size_t ctrl, x[2], ids[2], w[2], ids_loc[2], w_loc[2], recv[2], ws[2], total;
     Layout L;  // the local forward over world * tokens_cap tokens
 };
 
@@ -197,6 +199,7 @@ static PeerLayout make_peer_layout(int world, int tcap, int k, int e_loc, int H,
         P.w[p] = take(n * 4);
         P.ids_loc[p] = take(nl * 8);
         P.w_loc[p] = take(nl * 4);
+        P.recv[p] = take(n * H * 2);   // expert output rows of this rank's routes, slot t * k + j
         P.ws[p] = take(P.L.total);
     }
     P.total = o;
@@ -312,7 +315,7 @@ static void timer_end(cudaStream_t st)
 static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuffers& pb, __half* xt_g, __half* xt_u,
                                      __half* xt_d, __half* y, float* partials, int* counters, int* status, int split,
                                      int groups_bound, int rows_bound, float limit, int fat, uint8_t* gemm_scratch,
-                                     cudaStream_t st)
+                                     cudaStream_t st, const RowPush& push = RowPush{})
 {
     const int H = layer->hidden, I = layer->intermediate;
     // an expert takes the GEMM path with more than `fat` rows; no expert has more rows than the call's
@@ -336,6 +339,7 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
     ga.xt_u = xt_u;
     ga.xt_d = xt_d;
     ga.y = y;
+    ga.push = push;
     ga.rows_bound = rows_bound;
     ga.limit = limit;
     ga.scratch = gemm_scratch;
@@ -367,6 +371,7 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
     gd.svh_a = static_cast<const __half*>(layer->w2_svh);
     gd.suh_d = nullptr;
     gd.out = y;
+    gd.push = push;
     gd.K = I;
     gd.N = H;
     if (split == 1) {
@@ -561,25 +566,32 @@ int dsv41_ep_peer_forward(const dsv41_moe_layer* local_layer, const dsv41_ep_pee
     int* xstatus = reinterpret_cast<int*>(own + P.ctrl + kCtrlStatus);
     void* ws = own + P.ws[p];
     cudaError_t err;
-    timer_begin(st);  // stages as dsv41_moe_forward; permute includes publish + gather, combine the pull
-    // 1. publish this rank's tokens, then stamp in_flag[rank] on every peer
+    timer_begin(st);  // stages as dsv41_moe_forward; permute includes publish + gather, combine the wait + sum
+    // 1. publish this rank's tokens; the launch's last block stamps in_flag[rank] on every peer
     if ((err = launch_ep_publish(x, x_dtype, ids, weights, T, tcap, k, E, H, reinterpret_cast<__half*>(own + P.x[p]),
-                                 reinterpret_cast<int*>(own + P.ids[p]), reinterpret_cast<float*>(own + P.w[p]), st)) !=
-        cudaSuccess)
+                                 reinterpret_cast<int*>(own + P.ids[p]), reinterpret_cast<float*>(own + P.w[p]), peers,
+                                 world, rank, P.ctrl + kCtrlInFlags, stamp,
+                                 reinterpret_cast<int*>(own + P.ctrl + kCtrlPubDone), st)) != cudaSuccess)
         return cuda_fail(err, "ep publish");
-    if ((err = launch_ep_signal(peers, world, rank, P.ctrl + kCtrlInFlags, stamp, st)) != cudaSuccess)
-        return cuda_fail(err, "ep signal in");
-    // 2. every peer's routes that land on this rank's experts
-    int64_t* ids_loc = reinterpret_cast<int64_t*>(own + P.ids_loc[p]);
-    float* w_loc = reinterpret_cast<float*>(own + P.w_loc[p]);
-    if ((err = launch_ep_gather(peers, world, rank, tcap, k, rank * e_loc, (rank + 1) * e_loc, stamp,
-                                P.ctrl + kCtrlInFlags, P.ids[p], P.w[p], ids_loc, w_loc, xstatus, peer_wait_limit_ns(g),
-                                st)) != cudaSuccess)
-        return cuda_fail(err, "ep gather");
-    // 3. the local forward over world * tcap tokens, token rows read from their ranks
+    // 2. every peer's routes that land on this rank's experts (after a bounded wait for the in-stamps),
+    // 3. permuted: one launch when the single-CTA permutation applies
+    EpGather eg{};
+    eg.peers = peers;
+    eg.in_flags = reinterpret_cast<const uint32_t*>(own + P.ctrl + kCtrlInFlags);
+    eg.ids_off = P.ids[p];
+    eg.w_off = P.w[p];
+    eg.ids_out = reinterpret_cast<int64_t*>(own + P.ids_loc[p]);
+    eg.w_out = reinterpret_cast<float*>(own + P.w_loc[p]);
+    eg.world = world;
+    eg.per = tcap * k;
+    eg.lo = rank * e_loc;
+    eg.hi = (rank + 1) * e_loc;
+    eg.stamp = stamp;
+    eg.status = xstatus;
+    eg.limit_ns = peer_wait_limit_ns(g);
     const PermBuffers pb = perm_buffers(ws, L);
-    if ((err = launch_permute(ids_loc, w_loc, L.N, k, e_loc, nullptr, 0, fat, pb, st)) != cudaSuccess)
-        return cuda_fail(err, "permute");
+    if ((err = launch_permute_gathered(eg, k, e_loc, fat, pb, st)) != cudaSuccess)
+        return cuda_fail(err, "ep gather + permute");
     timer_mark(st, 1);
     XRows xr{};
     for (int d = 0; d < world; ++d) xr.base[d] = static_cast<const uint8_t*>(g->bases[d]) + P.x[p];
@@ -590,19 +602,26 @@ int dsv41_ep_peer_forward(const dsv41_moe_layer* local_layer, const dsv41_ep_pee
                                 at<__half>(ws, L.xt_u), gemm_sums(ws, L, fat), st)) != cudaSuccess)
         return cuda_fail(err, "prep");
     timer_mark(st, 2);
+    // 4. the expert passes; the down pass stores each output row into its token owner's receive slot
+    RowPush push{};
+    for (int d = 0; d < world; ++d) push.base[d] = static_cast<uint8_t*>(g->bases[d]) + P.recv[p];
+    push.route = pb.route_sorted;
+    push.per = tcap * k;
     if ((err = run_expert_passes(local_layer, pb, at<__half>(ws, L.xt_g), at<__half>(ws, L.xt_u),
                                  at<__half>(ws, L.xt_d), at<__half>(ws, L.y), at<float>(ws, L.partials),
                                  at<int>(ws, L.counters), at<int>(ws, L.status), L.split, L.groups_bound, L.rows, limit,
-                                 fat, at<uint8_t>(ws, L.gemm), st)) != cudaSuccess)
+                                 fat, at<uint8_t>(ws, L.gemm), st, push)) != cudaSuccess)
         return cuda_fail(err, "expert passes");
-    // 4. outputs ready: stamp out_flag[rank] on every peer; 5. pull this rank's routes' outputs
-    if ((err = launch_ep_signal(peers, world, rank, P.ctrl + kCtrlOutFlags, stamp, st)) != cudaSuccess)
+    // 5. outputs delivered: drop flag + out stamp on every peer; 6. sum this rank's routes from its slots
+    if ((err = launch_ep_signal(peers, world, rank, P.ctrl + kCtrlOutFlags, stamp, pb.nrows, P.ctrl + kCtrlOutDrop,
+                                st)) != cudaSuccess)
         return cuda_fail(err, "ep signal out");
     if (T > 0 &&
-        (err = launch_ep_combine(peers, world, rank, tcap, k, e_loc, stamp, P.ctrl + kCtrlOutFlags,
+        (err = launch_ep_combine(reinterpret_cast<const uint32_t*>(own + P.ctrl + kCtrlOutFlags),
+                                 reinterpret_cast<const uint32_t*>(own + P.ctrl + kCtrlOutDrop), world, e_loc, stamp,
                                  reinterpret_cast<const int*>(own + P.ids[p]), reinterpret_cast<const float*>(own + P.w[p]),
-                                 T, H, P.ws[p] + L.route_pos, P.ws[p] + L.y, out, xstatus, peer_wait_limit_ns(g),
-                                 st)) != cudaSuccess)
+                                 T, k, H, reinterpret_cast<const __half*>(own + P.recv[p]), out, xstatus,
+                                 peer_wait_limit_ns(g), st)) != cudaSuccess)
         return cuda_fail(err, "ep combine");
     timer_end(st);
     return DSV41_OK;

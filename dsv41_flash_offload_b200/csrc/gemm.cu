@@ -113,6 +113,7 @@ struct GemmParams {
     const __half* svh_a;    // gate/up: w13_svh [E][2][N]; down: w2_svh [E][N]
     const __half* suh_d;    // gate/up: w2_suh [E][N]
     __half* out;            // gate/up: xt_d [rows][N]; down: y [rows][N]
+    RowPush push;           // down under expert-parallel push: where each row goes instead of out
     const float* rs;        // activation sums per sorted row: gate/up [2 rows] (gate, up); down [rows][K/128]
     float* xs_out;          // gate/up: block sums of the stored down inputs [rows][N/128]
     int* status;
@@ -598,15 +599,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 // the row's input sum(s) of the affine form (rows past the pass are never stored)
                 const bool live = row < rows;
                 const size_t grow = (size_t)(row0 + row);
+                __half* dst = nullptr;   // the row's 128 outputs (resolved while few registers are live)
                 if (MODE == 0) {
                     const uint32_t colg = (uint32_t)((mt * 2 + 0) * kBN), colu = (uint32_t)((mt * 2 + 1) * kBN);
                     const __half* svg = p.svh_a + (size_t)e * 2 * p.N + fb * kBN;
                     gateup_epilogue(v, lane_addr + colg, lane_addr + colu, svg, svg + p.N,
                                     p.suh_d + (size_t)e * p.N + fb * kBN, p.limit, live ? p.rs + 2 * grow : nullptr);
+                    dst = p.out + grow * p.N + fb * kBN;
                 } else {
                     float xs = 0.0f;
-                    if (live)
+                    if (live) {
                         for (int b = 0; b < p.K / 128; ++b) xs += p.rs[grow * (p.K / 128) + b];
+                        dst = out_row(p.out, p.push, row0 + row, p.N) + fb * kBN;
+                    }
                     tmem_ld128(lane_addr + (uint32_t)(mt * kBN), v);
 #pragma unroll
                     for (int i = 0; i < 128; ++i) v[i] = fmaf(kKinv, v[i], kKbias * xs);
@@ -614,7 +619,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 }
                 if (live) {
                     // 256 B of the row as eight 32-byte stores (rows are 4-8 KB, blocks 256 B: 32-byte aligned)
-                    __half* dst = p.out + (size_t)(row0 + row) * p.N + fb * kBN;
                     float bs = 0.0f;   // gate/up: block sum of the stored down inputs (the down pass's affine form)
 #pragma unroll
                     for (int c16 = 0; c16 < 8; ++c16) {
@@ -625,7 +629,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                             if (MODE == 0) bs += __low2float(h) + __high2float(h);
                             o[j] = half2_as_u32(h);
                         }
-                        st_global_32B(dst + c16 * 16, o);
+                        if (MODE == 1 && p.push.route) {
+                            // a peer's receive slot: 16-byte stores over NVLink
+                            *reinterpret_cast<uint4*>(dst + c16 * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+                            *reinterpret_cast<uint4*>(dst + c16 * 16 + 8) = make_uint4(o[4], o[5], o[6], o[7]);
+                        } else {
+                            st_global_32B(dst + c16 * 16, o);
+                        }
                     }
                     if (MODE == 0) p.xs_out[grow * (p.N / kBN) + fb] = bs;
                 }
@@ -633,6 +643,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
             tc_fence_before();
         }
     }
+    // output rows stored into peers' memory are visible at system scope before the kernel ends
+    if (MODE == 1 && p.push.route) __threadfence_system();
     __syncthreads();
     if (warp == kWarpMma) {
         tc_fence_after();
@@ -752,6 +764,7 @@ static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
         p.svh_a = static_cast<const __half*>(a.layer->w2_svh);
         p.suh_d = nullptr;
         p.out = a.y;
+        p.push = a.push;
         p.rs = gemm_down_sums(a.scratch, N, E);
         p.xs_out = nullptr;
         p.K = I;

@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include "../../include/dsv41_b200.h"
+#include "internal.h"
 
 namespace dsv41 {
 
@@ -21,6 +22,7 @@ struct GemmArgs {
     const __half* xt_u;      // [rows][H]
     __half* xt_d;            // [rows][I] down inputs (written by gate/up, read by down)
     __half* y;               // [rows][H] expert outputs (written by down)
+    RowPush push;            // expert-parallel push: the down rows go to their token owners instead of y
     int rows_bound;          // upper bound of the total sorted rows
     float limit;
     uint8_t* scratch;

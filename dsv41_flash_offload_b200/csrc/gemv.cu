@@ -375,9 +375,10 @@ __device__ __forceinline__ void gemv_consume(const GemvParams& p, GemvSmem<K, ST
     // up on a wait, its remaining rows are written as zeros (the status word says why).
     const bool aborted = *reinterpret_cast<volatile int*>(&S.abort_flag) != 0;
     for (int j = warp; j < rows; j += kConsumerWarps) {
+        __half* orow = out_row(p.out, p.push, row0 + j, p.N);
         if (aborted) {
             for (int c = lane * 4; c < cols; c += 128)
-                *reinterpret_cast<uint2*>(p.out + (size_t)(row0 + j) * p.N + cb * cols + c) = make_uint2(0u, 0u);
+                *reinterpret_cast<uint2*>(orow + cb * cols + c) = make_uint2(0u, 0u);
             continue;
         }
         if (MODE == 0) {
@@ -400,7 +401,7 @@ __device__ __forceinline__ void gemv_consume(const GemvParams& p, GemvSmem<K, ST
             uint2 o;
             o.x = half2_as_u32(__floats2half2_rn(__fmul_rn(v[0], kHad), __fmul_rn(v[1], kHad)));
             o.y = half2_as_u32(__floats2half2_rn(__fmul_rn(v[2], kHad), __fmul_rn(v[3], kHad)));
-            *reinterpret_cast<uint2*>(p.out + (size_t)(row0 + j) * p.N + cb * 128 + lane * 4) = o;
+            *reinterpret_cast<uint2*>(orow + cb * 128 + lane * 4) = o;
         } else {
 #pragma unroll
             for (int blk = 0; blk < 2; ++blk) {
@@ -412,7 +413,7 @@ __device__ __forceinline__ void gemv_consume(const GemvParams& p, GemvSmem<K, ST
                 uint2 o;
                 o.x = half2_as_u32(__floats2half2_rn(y[0], y[1]));
                 o.y = half2_as_u32(__floats2half2_rn(y[2], y[3]));
-                *reinterpret_cast<uint2*>(p.out + (size_t)(row0 + j) * p.N + c) = o;
+                *reinterpret_cast<uint2*>(orow + c) = o;
             }
         }
     }
@@ -521,6 +522,9 @@ __global__ void __launch_bounds__(gemv_threads<KS>(), KS == 1 ? DSV41_GEMV_MIN_B
         else
             gemv_consume<1, K, KS, kStages>(w.p[1], S, u, it, warp, lane, lw, nullptr);
     }
+    // output rows stored into peers' memory are made visible at system scope before the kernel ends (the
+    // exchange's release stamp follows on the stream)
+    if (w.p[1].push.route) __threadfence_system();
 }
 
 int gemv_units_bound(int groups_bound, int K, int N, int mode, int split)

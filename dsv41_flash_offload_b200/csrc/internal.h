@@ -22,6 +22,39 @@ struct XRows {
     const void* base[kMaxPeers];
     int per, n;
 };
+// Where an expert pass stores its output rows. route == nullptr: the pass's own output array, row r at
+// out + r * N. Otherwise (expert-parallel push): sorted row r serves flat route i = route[r] of rank
+// d = i / per, and its output row goes straight into that rank's receive slots, base[d] + (i % per) rows --
+// a peer store over NVLink issued by the epilogue, so the combine exchange overlaps the expert math.
+struct RowPush {
+    void* base[kMaxPeers];
+    const int* route;
+    int per;
+};
+#ifdef __CUDACC__
+__device__ __forceinline__ __half* out_row(__half* out, const RowPush& push, int row, int N)
+{
+    if (!push.route) return out + (size_t)row * N;
+    const int i = push.route[row];
+    const int d = i / push.per;
+    return static_cast<__half*>(push.base[d]) + (size_t)(i - d * push.per) * N;
+}
+#endif
+
+// Expert-parallel gather: after a bounded wait for every peer's in-stamp, the routes of experts [lo, hi)
+// from every peer's published id/weight tables (per entries each, at ids_off / w_off of its buffer), as
+// local ids (-1 for other ranks' experts) and weights in ids_out / w_out [world * per]
+struct EpGather {
+    PeerTable peers;
+    const uint32_t* in_flags;   // this rank's in_flag[world]
+    size_t ids_off, w_off;
+    int64_t* ids_out;
+    float* w_out;
+    int world, per, lo, hi;
+    uint32_t stamp;
+    int* status;
+    uint64_t limit_ns;
+};
 
 // Routing permutation results (device pointers; int32 internally)
 struct PermBuffers {
@@ -51,6 +84,10 @@ int max_groups(int N, int E);
 cudaError_t launch_permute(const int64_t* ids, const float* weights, int N, int topk, int E,
                            const int32_t* expert_map, int map_len, int fat_threshold,
                            const PermBuffers& pb, cudaStream_t st);
+// the expert-parallel gather followed by the permutation of the gathered routes (N = world * per); when
+// the single-CTA permutation applies, the gather runs inside it (one launch)
+cudaError_t launch_permute_gathered(const EpGather& g, int topk, int E, int fat_threshold, const PermBuffers& pb,
+                                    cudaStream_t st);
 
 // rsum (optional, [2 * N] fp32): per sorted row, the sums of the row's stored xt_g / xt_u values
 cudaError_t launch_prep(const void* x, int x_dtype, const int* token_sorted, const int* expert_sorted,
@@ -62,16 +99,19 @@ cudaError_t launch_router_topk(const void* logits, int logits_dtype, int T, int 
 cudaError_t launch_prep_rows(const XRows& x, int x_dtype, const int* token_sorted, const int* expert_sorted,
                              const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
                              float* rsum, cudaStream_t st);
+// publish this rank's tokens, ids and weights, then (last block) stamp in_flag[rank] on every peer;
+// `done` is a zeroed int of this rank's control block (reset by the launch)
 cudaError_t launch_ep_publish(const void* x, int x_dtype, const int64_t* ids, const float* w, int T, int tcap, int k,
-                              int E, int H, __half* X, int* IDS, float* W, cudaStream_t st);
+                              int E, int H, __half* X, int* IDS, float* W, const PeerTable& peers, int world, int rank,
+                              size_t flag_off, uint32_t stamp, int* done, cudaStream_t st);
+// stamp flag_off[rank] on every peer; with nrows, first the drop flag drop_off[rank] (stamp if *nrows == 0)
 cudaError_t launch_ep_signal(const PeerTable& peers, int world, int rank, size_t flag_off, uint32_t stamp,
-                             cudaStream_t st);
-cudaError_t launch_ep_gather(const PeerTable& peers, int world, int rank, int tcap, int k, int lo, int hi,
-                             uint32_t stamp, size_t in_flags_off, size_t ids_off, size_t w_off, int64_t* ids_loc,
-                             float* w_loc, int* status, uint64_t limit_ns, cudaStream_t st);
-cudaError_t launch_ep_combine(const PeerTable& peers, int world, int rank, int tcap, int k, int e_loc, uint32_t stamp,
-                              size_t out_flags_off, const int* ids, const float* w, int T, int H, size_t route_pos_off,
-                              size_t y_off, float* out, int* status, uint64_t limit_ns, cudaStream_t st);
+                             const int* nrows, size_t drop_off, cudaStream_t st);
+cudaError_t launch_ep_gather(const EpGather& g, cudaStream_t st);
+// wait for every rank's out stamp, then out[t] = sum_j w[t, j] * recv[t * k + j] over live routes
+cudaError_t launch_ep_combine(const uint32_t* out_flags, const uint32_t* drops, int world, int e_loc, uint32_t stamp,
+                              const int* ids, const float* w, int T, int k, int H, const __half* recv, float* out,
+                              int* status, uint64_t limit_ns, cudaStream_t st);
 
 // Work lists for an explicit expert list over caller-permuted rows (run_batch semantics):
 // int32 counts/offsets copies, expert_sorted (-1 for rows of unlisted experts), GEMV groups of the
@@ -91,6 +131,7 @@ struct GemvParams {
     const __half* svh_a;   // gate/up pass: w13_svh [E][2][N]; down pass: w2_svh [E][N]
     const __half* suh_d;   // gate/up pass: w2_suh [E][N]
     __half* out;           // gate/up pass: xt_d [rows][N]; down pass: y [rows][N]
+    RowPush push;          // down pass under expert-parallel push: where each row goes instead of out
     float* partials;       // split-K partials [units][4096]
     int* counters;         // split-K arrival counters [units / split]
     int* status;

@@ -11,6 +11,7 @@
 // The same pass builds the work lists of the expert kernels: row groups of <= 16 rows for
 // experts on the decode-GEMV path, and the list of experts over fat_threshold rows (GEMM path).
 #include "common.cuh"
+#include "ep_device.cuh"
 #include "internal.h"
 
 namespace dsv41 {
@@ -74,6 +75,8 @@ struct PermArgs {
     int map_len;
     int fat;
     PermBuffers pb;
+    int gather;   // single-CTA path: first gather ids/w from the expert-parallel peers (g)
+    EpGather g;
 };
 
 // tot[e] (e <= E) holds the per-expert totals in shared memory; writes counts/offsets and the
@@ -172,6 +175,12 @@ __global__ void __launch_bounds__(1024) permute_small_kernel(const PermArgs a)
     int* tot = seg + 32 * E1;         // [E1]
     int* tmp = tot + E1;              // [E1]
     int* scratch = tmp + E1;          // [33]
+    if (a.gather) {
+        // expert parallel: the routes of this rank's experts from every peer's tables, into a.ids / a.w
+        const bool ok = block_wait_stamps(a.g.in_flags, a.g.world, a.g.stamp, a.g.status, a.g.limit_ns);
+        ep_gather_routes(a.g, ok, threadIdx.x, blockDim.x);
+        __syncthreads();
+    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = (a.N + 31) / 32;
     const int b = min(a.N, warp * S), e = min(a.N, b + S);
@@ -370,6 +379,26 @@ cudaError_t launch_permute(const int64_t* ids, const float* weights, int N, int 
     permute_scan_kernel<<<1, 1024, smem_s, st>>>(a);
     permute_scatter_kernel<<<blocks, kPermWarps * 32, smem_x, st>>>(a);
     return cudaGetLastError();
+}
+
+cudaError_t launch_permute_gathered(const EpGather& g, int topk, int E, int fat_threshold, const PermBuffers& pb,
+                                    cudaStream_t st)
+{
+    const int N = g.world * g.per;
+    if (perm_uses_small(N, E)) {
+        PermArgs a{g.ids_out, g.w_out, N, topk, E, nullptr, 0, fat_threshold, pb};
+        a.gather = 1;
+        a.g = g;
+        const size_t E1 = (size_t)E + 1;
+        const size_t smem = (32 * E1 + 2 * E1 + 33) * sizeof(int);
+        cudaError_t err;
+        if ((err = set_smem((const void*)permute_small_kernel, smem)) != cudaSuccess) return err;
+        permute_small_kernel<<<1, 1024, smem, st>>>(a);
+        return cudaGetLastError();
+    }
+    const cudaError_t err = launch_ep_gather(g, st);
+    if (err != cudaSuccess) return err;
+    return launch_permute(g.ids_out, g.w_out, N, topk, E, nullptr, 0, fat_threshold, pb, st);
 }
 
 }  // namespace dsv41

@@ -58,15 +58,18 @@ __device__ __forceinline__ void store8_half(__half* p, const float (&v)[8])
     *reinterpret_cast<uint4*>(p) = u;
 }
 
-// 128-point Hadamard of one block held by 4 lanes x 32 consecutive values (element 32*hl + q): stages
-// w = 1 .. 16 inside the thread, then w = 32, 64 across lanes hl ^ 1, hl ^ 2 -- the same pairs and order
-// as the reference's had128 (ft_core.h:89-94) with 2 of the 7 stages on the shuffle unit
-__device__ __forceinline__ void had128_quad(float (&v)[32], int hl)
+// 128-point Hadamard of one block held by L lanes x 128/L consecutive values (element (128/L)*hl + q):
+// stages w = 1 .. 64/L inside the thread, then w = 128/L .. 64 across lanes hl ^ 1, hl ^ 2, ... -- the
+// same pairs and order as the reference's had128 (ft_core.h:89-94), log2(L) of the 7 stages on the
+// shuffle unit
+template <int L>
+__device__ __forceinline__ void had128_lanes(float (&v)[128 / L], int hl)
 {
+    constexpr int V = 128 / L;
 #pragma unroll
-    for (int w = 1; w < 32; w <<= 1)
+    for (int w = 1; w < V; w <<= 1)
 #pragma unroll
-        for (int b = 0; b < 32; b += 2 * w)
+        for (int b = 0; b < V; b += 2 * w)
 #pragma unroll
             for (int i = b; i < b + w; ++i) {
                 const float a = v[i], c = v[i + w];
@@ -74,11 +77,11 @@ __device__ __forceinline__ void had128_quad(float (&v)[32], int hl)
                 v[i + w] = a - c;
             }
 #pragma unroll
-    for (int m = 1; m < 4; m <<= 1) {
+    for (int m = 1; m < L; m <<= 1) {
         // lower element: v + partner; upper: partner - v -- one FFMA with +-1 rounds exactly as the add
         const float sg = (hl & m) ? -1.0f : 1.0f;
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
+        for (int q = 0; q < V; ++q) {
             const float pv = __shfl_xor_sync(0xffffffffu, v[q], m);
             v[q] = fmaf(sg, v[q], pv);
         }
@@ -86,19 +89,26 @@ __device__ __forceinline__ void had128_quad(float (&v)[32], int hl)
 }
 
 // one warp per sorted row p (rows p < *nrows; rows whose expert_sorted entry is negative are skipped):
-// lanes 4g .. 4g+3 transform 128-block 8j + g of the row for gate and up,
+// lanes L*g .. L*g+L-1 transform 128-block (32/L)*j + g of the row for gate and up,
 //   xt_{g,u}[p] = fp16(H128(fp16(x[token]) * suh_{g,u}) * 2^-3.5)
 // with 16-byte loads and stores; the row's indices are read once. With rsum, it also writes the sums of
 // the stored (fp16) values of the row, rsum[2p] (gate) and rsum[2p + 1] (up), in fp32 in a fixed order:
 // the activation sums of the busy-expert GEMM's affine weight codes.
-__global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ XRows x, int x_dtype, const int* token_sorted,
-                                                   const int* expert_sorted, const int* nrows,
-                                                   const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
-                                                   float* rsum)
+#ifndef DSV41_PREP_LANES
+#define DSV41_PREP_LANES 4        // lanes per 128-block (4: 32 values per lane; 8: 16 values, fewer registers)
+#endif
+#ifndef DSV41_PREP_MIN_BLOCKS
+#define DSV41_PREP_MIN_BLOCKS 2   // resident blocks per SM the register allocation must allow
+#endif
+constexpr int kPrepLanes = DSV41_PREP_LANES;
+__global__ void __launch_bounds__(256, DSV41_PREP_MIN_BLOCKS)
+    prep_kernel(const __grid_constant__ XRows x, int x_dtype, const int* token_sorted, const int* expert_sorted,
+                const int* nrows, const __half* w13_suh, int H, __half* xt_g, __half* xt_u, float* rsum)
 {
-    const int lane = threadIdx.x & 31, hl = lane & 3, g = lane >> 2;
+    constexpr int L = kPrepLanes, V = 128 / L, BPW = 32 / L;   // lanes per block, values per lane, blocks per warp
+    const int lane = threadIdx.x & 31, hl = lane % L, g = lane / L;
     const int nvalid = *nrows;
-    const int nb = H / 128, nit = (nb + 7) / 8;
+    const int nb = H / 128, nit = (nb + BPW - 1) / BPW;
     const int wstride = gridDim.x * (blockDim.x >> 5);
     for (int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < nvalid; p += wstride) {
         const int e = expert_sorted[p];
@@ -114,12 +124,12 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ XRows
         const __half* sg = w13_suh + (size_t)e * 2 * H;
         float sum[2] = {0.0f, 0.0f};
         for (int j = 0; j < nit; ++j) {
-            const int blk = 8 * j + g;
+            const int blk = BPW * j + g;
             const bool act = blk < nb;   // lanes past the last block transform a copy of block 0, unstored
-            const int c = (act ? blk : 0) * 128 + hl * 32;
-            float xv[32];
+            const int c = (act ? blk : 0) * 128 + hl * V;
+            float xv[V];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < V / 8; ++k) {
                 float x8[8];
                 load8_as_half(xb, x_dtype, row * H + c + 8 * k, x8);
 #pragma unroll
@@ -127,18 +137,18 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ XRows
             }
 #pragma unroll
             for (int m = 0; m < 2; ++m) {
-                float v[32];
+                float v[V];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < V / 8; ++k) {
                     float sv[8];
                     load8_half(sg + (size_t)m * H + c + 8 * k, sv);
 #pragma unroll
                     for (int q = 0; q < 8; ++q) v[8 * k + q] = __fmul_rn(xv[8 * k + q], sv[q]);
                 }
-                had128_quad(v, hl);
+                had128_lanes<L>(v, hl);
                 __half* o = (m ? xt_u : xt_g) + (size_t)p * H + c;
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
+                for (int k = 0; k < V / 8; ++k) {
                     float w8[8];
 #pragma unroll
                     for (int q = 0; q < 8; ++q) w8[q] = __fmul_rn(v[8 * k + q], kHad);

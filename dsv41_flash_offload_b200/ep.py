@@ -160,10 +160,10 @@ class EPPeerMoE:
     Construction is collective over `group` (every rank must construct with the same arguments): the
     ranks allocate one shared device buffer each, exchange CUDA IPC handles over the process group
     (host side only) and map each other's buffers. A call runs one layer step for this rank's
-    T <= tokens_cap tokens: the row transform pulls each routed token row from its rank and the
-    combine pulls each expert output from the rank that computed it, both by plain peer loads,
-    ordered by step stamps in the shared buffers (bounded device waits; `read_status()` reports an
-    expired wait). Every rank must call once per step, in the same order. No host synchronisation:
+    T <= tokens_cap tokens: the row transform pulls each routed token row from its rank (peer loads)
+    and the down pass's epilogue stores each expert output row into its token owner's receive slot
+    (peer stores), ordered by step stamps in the shared buffers (bounded device waits; `read_status()`
+    reports an expired wait); the combine then sums the rank's own slots. Every rank must call once per step, in the same order. No host synchronisation:
     steps of equal parity can be captured in one CUDA graph.
     """
 

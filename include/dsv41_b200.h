@@ -201,9 +201,10 @@ int dsv41_moe_forward_logits(const dsv41_moe_layer* layer, const void* x, int32_
  * peers over the host, opens theirs (dsv41_ep_peer_open) and fills bases[] (own buffer at
  * bases[rank]). dsv41_ep_peer_forward then runs one step of the layer for this rank's T <=
  * tokens_cap tokens with no collective library: the row transform reads each routed token row
- * from its rank and the combine reads each expert output from the rank that computed it, both by
- * plain peer loads; step stamps in the shared buffers order the ranks (bounded waits, status 1
- * on expiry -> dsv41_ep_peer_read_status). Every rank must call it once per step with the same
+ * from its rank (plain peer loads) and the down pass stores each expert output row into the
+ * receive slot of its token's rank (plain peer stores), whose combine then sums its own slots;
+ * step stamps in the shared buffers order the ranks (bounded waits, status 1 on expiry ->
+ * dsv41_ep_peer_read_status). Every rank must call it once per step with the same
  * `step` sequence (0, 1, 2, ...), topk and tokens_cap. The buffers alternate by step parity, so a
  * CUDA graph of one step replays only for steps of the same parity. Hidden size up to 8192.
  * ------------------------------------------------------------------------------------------ */
