@@ -337,6 +337,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
         : "memory");
     return ok != 0;
 }
+// The same test, but a thread whose phase is not complete may be suspended in hardware until the
+// phase completes or about `hint_ns` have passed. A suspended warp issues nothing, so a waiting
+// producer / MMA / consumer warp leaves the sub-partition's issue slots to the warps that decode
+// (measured: the plain try_wait polling loop cost ~0.7 try_waits per decoded tile in the GEMV and
+// ~4 in the GEMM, with their branches and yields around them).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ uint64_t globaltimer_ns()
 {
     uint64_t t;
@@ -345,17 +360,27 @@ __device__ __forceinline__ uint64_t globaltimer_ns()
 }
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s, as the reference's combine wait
+#ifndef DSV41_WAIT_HINT_NS
+#define DSV41_WAIT_HINT_NS 20000   // suspend hint of one try_wait (0: poll without suspending)
+#endif
 
 // Wait for phase `parity` of `bar`. Returns false (and records kStatusWaitTimeout) if it has
 // not completed within `limit_ns` (default kWaitLimitNs) or if `abort_flag` is already set.
+// Each retry may sleep up to DSV41_WAIT_HINT_NS in hardware, so the limit and the abort flag are
+// checked after every retry; a wait therefore ends at most one hint after its limit.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
                                                   uint64_t limit_ns = kWaitLimitNs)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
+#if DSV41_WAIT_HINT_NS > 0
+        if (mbar_try_wait_hint(bar, parity, DSV41_WAIT_HINT_NS)) return true;
+        {
+#else
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63u) == 0) {
+#endif
             if (*abort_flag) return false;
             if (globaltimer_ns() - t0 > limit_ns) {
                 *abort_flag = 1;

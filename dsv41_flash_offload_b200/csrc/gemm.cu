@@ -46,6 +46,9 @@ constexpr int kGemmThreads = (kWarpDec0 + kDecWarps) * 32;   // 384
 #define DSV41_GEMM_DEC_UNROLL 4
 #endif
 constexpr int kDecUnroll = DSV41_GEMM_DEC_UNROLL;   // tiles of the decode loop in flight per warp
+#ifndef DSV41_GEMM_IMAD_PACKS
+#define DSV41_GEMM_IMAD_PACKS 4   // of the 4 half2 code packs per lane and tile, how many on IMAD
+#endif
 #ifndef DSV41_GEMM_MERGED_RING
 #define DSV41_GEMM_MERGED_RING 1
 #endif
@@ -565,7 +568,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 for (int j = 0; j < ntn; ++j) {
                     const uint32_t* tw = trw + (nt0 + j) * TileFmt<K>::words;
                     uint32_t b[4];
-                    decode_tile_codes<K, 4>(tw, lw, k16, b);   // affine codes: the epilogue applies KINV, KBIAS
+                    decode_tile_codes<K, DSV41_GEMM_IMAD_PACKS>(tw, lw, k16, b);   // affine codes: the epilogue applies KINV, KBIAS
                     stmatrix_x4(bt + j * 2 * kAtom, b);
                 }
                 fence_async_smem();

@@ -95,10 +95,10 @@ __device__ __forceinline__ void had128_lanes(float (&v)[128 / L], int hl)
 // the stored (fp16) values of the row, rsum[2p] (gate) and rsum[2p + 1] (up), in fp32 in a fixed order:
 // the activation sums of the busy-expert GEMM's affine weight codes.
 #ifndef DSV41_PREP_LANES
-#define DSV41_PREP_LANES 4        // lanes per 128-block (4: 32 values per lane; 8: 16 values, fewer registers)
+#define DSV41_PREP_LANES 8        // lanes per 128-block (4: 32 values per lane; 8: 16 values, fewer registers)
 #endif
 #ifndef DSV41_PREP_MIN_BLOCKS
-#define DSV41_PREP_MIN_BLOCKS 2   // resident blocks per SM the register allocation must allow
+#define DSV41_PREP_MIN_BLOCKS 4   // resident blocks per SM (measured on the 16k prefill: 4 lanes x 2 blocks 1.07 ms, 8 x 3 0.93, 8 x 4 0.87)
 #endif
 constexpr int kPrepLanes = DSV41_PREP_LANES;
 __global__ void __launch_bounds__(256, DSV41_PREP_MIN_BLOCKS)
