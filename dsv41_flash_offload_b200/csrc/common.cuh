@@ -113,6 +113,8 @@ template <int K>
 struct LaneDec {
     int q0, q1, q2;
     uint32_t r;   // K = 3: left funnel shift of the window; K = 2, 4: shift of state 0
+    int c0, c1;   // K = 3, affine codes: the two words that hold the lane's 37 stream bits
+    uint32_t cs;  //                      and the right shift that puts them at bits [0, 37)
 };
 
 template <int K>
@@ -125,6 +127,12 @@ __device__ __forceinline__ LaneDec<K> lane_dec_setup(int t)
         d.q1 = w.q1;
         d.q2 = w.q2;
         d.r = w.r8;
+        // lane t's 8 states cover stream bits [24t - 13, 24t + 24) (mod 768): 37 bits starting at bit
+        // p = (24t - 13) mod 32 of word a, and p is 3, 11, 19 or 27, so they always lie in words a, a + 1
+        const int sb = (24 * t - 13 + 768) % 768;
+        d.c0 = sb >> 5;
+        d.c1 = (d.c0 + 1) % kTileWords;
+        d.cs = 27u - (uint32_t)(sb & 31);
     } else if constexpr (K == 4) {
         d.q0 = (t + 31) & 31;
         d.q1 = t;
@@ -169,6 +177,9 @@ __device__ __forceinline__ void decode_tile(const uint32_t* tw, const LaneDec<K>
 // of each weight (a half-ulp, 2^-11 relative). `kImadPacks` of the 4 half2 packs per lane go to the
 // IMAD pipe (c1 * 65536 + c0), the rest to PRMT, to balance the two integer pipes.
 // ------------------------------------------------------------------------------------------
+#ifndef DSV41_CODES_WIN2
+#define DSV41_CODES_WIN2 1   // K = 3 codes: the lane's states from two staged words (1: two loads, 0: three)
+#endif
 constexpr float kKinv = 0.00676727294921875f;   // fp16 0x1eee = 1774 * 2^-18 (exact)
 constexpr float kKbias = -10.3828125f;          // fp16 0xc931 = -1329 * 2^-7 (exact)
 
@@ -178,6 +189,18 @@ __device__ __forceinline__ void decode_tile_codes(const uint32_t* tw, const Lane
 {
     uint32_t s[8];
     if constexpr (K == 3) {
+#if DSV41_CODES_WIN2
+        // two words (MSB-first: word c0 is the high half), shifted right by cs: the lane's 37 bits at
+        // [0, 37) of (hi:lo), state j at bits [21 - 3j, 37 - 3j) for every lane
+        const uint32_t w0 = tw[d.c0], w1 = tw[d.c1];
+        const uint32_t hi = w0 >> d.cs;
+        const uint32_t lo = __funnelshift_r(w1, w0, d.cs);
+        s[0] = __funnelshift_r(lo, hi, 21) & 0xffffu;
+        s[1] = __funnelshift_r(lo, hi, 18) & 0xffffu;
+#pragma unroll
+        for (int j = 2; j < 7; ++j) s[j] = (lo >> (21 - 3 * j)) & 0xffffu;
+        s[7] = lo & 0xffffu;
+#else
         const uint32_t hi = __funnelshift_l(tw[d.q1], tw[d.q0], d.r);
         const uint32_t lo = __funnelshift_l(tw[d.q2], tw[d.q1], d.r);
 #pragma unroll
@@ -185,6 +208,7 @@ __device__ __forceinline__ void decode_tile_codes(const uint32_t* tw, const Lane
         s[5] = (lo >> 14) & 0xffffu;
         s[6] = (lo >> 11) & 0xffffu;
         s[7] = __byte_perm(lo, 0u, 0x4421);
+#endif
     } else {
         const uint32_t hi = tw[d.q0], lo = tw[d.q1];
 #pragma unroll
