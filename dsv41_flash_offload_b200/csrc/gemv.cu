@@ -59,6 +59,11 @@ namespace dsv41 {
 #define DSV41_GEMV_IMAD_PACKS 3       // of the 4 half2 code packs per lane and tile, how many on IMAD (measured 2: 1.577, 3: 1.556, 4: 1.576 ms GEMV at T=64)
 #endif
 
+#ifndef DSV41_GEMV_ROW_UNROLL
+#define DSV41_GEMV_ROW_UNROLL 16      // k-rows of a stage unrolled in the consumer loop
+#endif
+constexpr int kRowUnroll = DSV41_GEMV_ROW_UNROLL;
+
 #ifndef DSV41_GEMV_TILES_PER_WARP
 #define DSV41_GEMV_TILES_PER_WARP 2   // adjacent n-tiles per consumer warp (they share the A fragment)
 #endif
@@ -130,7 +135,7 @@ __device__ __forceinline__ void gemv_stage(const uint32_t* trow, uint32_t xaddr,
                                                    float (&rs)[2][4], int par)
 {
     constexpr int kTW = TileFmt<K>::words, kRowWords = row_bytes<K>() / 4;
-#pragma unroll
+#pragma unroll kRowUnroll
     for (int r0 = 0; r0 < kStageRows; r0 += KS) {
         const int r = r0 + par;
         uint32_t bx[4];
