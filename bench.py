@@ -18,6 +18,8 @@ roofline= the dominant kernel (decode-GEMV gate/up pass): algorithmic bytes (dis
           experts' gate+up trellis and scales, activations in, down-input out) / its average
           duration from CUDA events on its own stream inside the timed region, against the
           measured HBM copy bandwidth (MEASURED_PEAKS.json)
+sweep   = (N=1) decode T = 1/8/32/64 through the same call, timed as eager calls and as replays of
+          CUDA graphs of those calls (graph_*: the serving form, without the host's per-call work)
 cpu_baseline / --impl reference = the reference's own AVX2 CPU expert tier
           (kernels/cpu_avx2/ft_tier_ext.cpp tier_forward, built into oracle/_ref) on the same
           decode batches, all host cores, rank 0 only.
@@ -27,7 +29,8 @@ layer kernels (--ep peer, default) or by fixed-slot NCCL all-to-all (--ep nccl),
 line then carries `ep_parity` (the first batch through the peer and NCCL paths vs the single-GPU
 layer of all experts on every rank; the run exits 3 if either is outside the parity bar), and `ep40` /
 `prefill_ep`: BASELINE configs[3] (40-layer stack, 256-token decode batch) and configs[4] (131,072
-tokens x 8 layers, Zipf(1.5)) measured in the same process (strong scaling; --no-stack skips them).
+tokens x 8 layers, Zipf(1.5); compact NCCL all-to-all, or the peer path with --prefill-exchange peer)
+measured in the same process (strong scaling; --no-stack skips them).
 --workload ep40 / prefill-ep run configs[3] / configs[4] alone as the line.
 """
 from __future__ import annotations
@@ -89,8 +92,11 @@ def parse():
                          "batch, GEMM tensor roofline); ep40: configs[3] 40-layer stack, 256-token decode batch; "
                          "prefill-ep: configs[4] 131,072 tokens x 8 layers, Zipf(1.5)")
     ap.add_argument("--ep", choices=["peer", "nccl"], default="peer",
-                    help="N > 1 decode exchange: peer = token rows and expert outputs read from peers' memory inside "
-                         "the row transform and combine kernels (EPPeerMoE); nccl = fixed-slot all-to-all (EPMoE)")
+                    help="N > 1 decode exchange (one layer and the configs[3] stack): peer = token rows read from "
+                         "peers' memory by the row transform and expert outputs stored into the token owners' memory "
+                         "by the down pass (EPPeerMoE); nccl = fixed-slot NCCL all-to-all (EPMoE)")
+    ap.add_argument("--prefill-exchange", choices=["nccl", "peer"], default="nccl",
+                    help="N > 1 configs[4] stack exchange: nccl = compact NCCL all-to-all (EPMoE); peer = EPPeerMoE")
     ap.add_argument("--prefill-tokens", type=int, default=16384, help="--workload prefill: tokens per batch")
     ap.add_argument("--experts", type=int, default=E,
                     help="--workload prefill: experts in the layer (fewer = a smaller case for profiling)")
@@ -450,9 +456,12 @@ def stack_measure(a, kind, world, rank, dev, dist_on, hbm):
     lo, hi = rank * e_loc, (rank + 1) * e_loc
     layers = [exl3.Exl3MoELayer.synthetic(E, H, I, seed=0, layer=l, device=dev,
                                           expert_range=(lo, hi) if world > 1 else None) for l in range(n_layers)]
-    # decode stack: peer-memory exchange (one set of shared buffers for all layers); prefill: NCCL
-    # all-to-all with compact (deduplicated) dispatch
-    peer = EPPeerMoE(layers[0], E, T, TOPK, limit=LIMIT) if kind == "ep40" and world > 1 and a.ep == "peer" else None
+    # decode stack: peer-memory exchange (--ep; one set of shared buffers for all layers); prefill stack:
+    # --prefill-exchange, NCCL all-to-all with compact (deduplicated) dispatch by default. Measured at N=2
+    # (131,072 tokens, 8 layers): NCCL 376.6 ms per step, peer 395.5 ms -- the peer path moves every route's
+    # token row (4.2M routes served per rank) where the compact dispatch sends each token once per rank (1.05M)
+    exchange = a.ep if kind == "ep40" else a.prefill_exchange
+    peer = EPPeerMoE(layers[0], E, T, TOPK, limit=LIMIT) if world > 1 and exchange == "peer" else None
     eps = [] if peer is not None else [EPMoE(local_layer_fn(lay, LIMIT), E) for lay in layers]
     if kind == "ep40":
         for ep in eps:
@@ -495,17 +504,19 @@ def stack_measure(a, kind, world, rank, dev, dist_on, hbm):
         gemv_frac = None
     if peer is not None:
         # routes each rank serves (summed over all ranks' tokens and all layers) and the bytes this rank
-        # pulls: token rows of the routes it serves + expert outputs of its own valid routes
-        dest = np.zeros(world)
+        # moves: token rows of the routes it serves + expert outputs of its own valid routes (each rank
+        # counts where its own routes go; one all-gather of the counts)
+        mine = np.zeros(world)
         own = 0
-        for l in range(n_layers):
-            for r in range(world):
-                v = all_ids[l][r].reshape(-1)
-                v = v[(v >= 0) & (v < E)]
-                dest += np.bincount(v // e_loc, minlength=world)[:world]
-                if r == rank:
-                    own += int(v.size)
-        recv = float(dest[rank])
+        for ids_l, _ in routes_np:
+            v = ids_l.reshape(-1)
+            v = v[(v >= 0) & (v < E)]
+            mine += np.bincount(v // e_loc, minlength=world)[:world]
+            own += int(v.size)
+        cnt = torch.tensor(mine, dtype=torch.float64, device=dev)
+        cnts = [torch.zeros_like(cnt) for _ in range(world)]
+        torch.distributed.all_gather(cnts, cnt)
+        recv = float(sum(float(c[rank]) for c in cnts))
         a2a = (recv + own) * H * 2
         peer.close()
     t = torch.tensor([recv, a2a, local_ms], dtype=torch.float64, device=dev)
@@ -767,9 +778,26 @@ def main():
             n = 100
             sms = time_steps(sstep, n, 5, dist_on)
             sst = stage_times(sstep, 64, 2)
+            # the same calls replayed from CUDA graphs (the serving form: vLLM captures its decode steps),
+            # i.e. without the host's per-call work between the launches
+            gstream = torch.cuda.Stream(dev)
+            gstream.wait_stream(torch.cuda.current_stream(dev))
+            graphs = []
+            with torch.cuda.stream(gstream):
+                for b in range(len(bs)):
+                    sstep(b)   # eager once on this stream: sizes its workspace before the capture
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=gstream):
+                        sstep(b)
+                    graphs.append(g)
+            torch.cuda.current_stream(dev).wait_stream(gstream)
+            gms = time_steps(lambda i, gs=graphs: gs[i % len(gs)].replay(), n, 5, dist_on)
+            del graphs
             lbs = statistics.mean(layer_bytes(ids, Ts) for _, ids, _ in hbs)
             gbs = statistics.mean(gemv_bytes(ids, Ts)[0] for _, ids, _ in hbs)
             sweep[str(Ts)] = {"tok_s": round(world * Ts * n / (sms / 1e3), 1), "ms_per_step": round(sms / n, 5),
+                              "graph_tok_s": round(world * Ts * n / (gms / 1e3), 1),
+                              "graph_ms_per_step": round(gms / n, 5),
                               "layer_hbm_frac": round(lbs / (sms / n / 1e3) / 1e9 / hbm, 4),
                               "gemv_hbm_frac": round(gbs / ((sst["gemv"] + sst["gemv_down"]) / 1e3) / 1e9 / hbm, 4)}
         line["sweep"] = sweep

@@ -177,7 +177,7 @@ constexpr size_t kCtrlOutDrop = 160;   // uint32 out_drop[kMaxPeers]: stamp of a
 constexpr size_t kCtrlPubDone = 224;   // int: blocks of this rank's publish launch that finished
 
 struct PeerLayout {
-    size_t ctrl, x[2], ids[2], w[2], ids_loc[2], w_loc[2], recv[2], ws[2], total;
+    size_t ctrl, x[2], ids[2], w[2], ids_loc[2], w_loc[2], recv[2], ws, total;
     Layout L;  // the local forward over world * tokens_cap tokens
 };
 
@@ -200,8 +200,10 @@ static PeerLayout make_peer_layout(int world, int tcap, int k, int e_loc, int H,
         P.ids_loc[p] = take(nl * 8);
         P.w_loc[p] = take(nl * 4);
         P.recv[p] = take(n * H * 2);   // expert output rows of this rank's routes, slot t * k + j
-        P.ws[p] = take(P.L.total);
     }
+    // the local forward's workspace: only this rank's own kernels touch it, in stream order, so one copy
+    // serves both parities (peers read x / ids / w and write recv, never the workspace)
+    P.ws = take(P.L.total);
     P.total = o;
     return P;
 }
@@ -564,7 +566,7 @@ int dsv41_ep_peer_forward(const dsv41_moe_layer* local_layer, const dsv41_ep_pee
     for (int d = 0; d < world; ++d) peers.base[d] = g->bases[d];
     uint8_t* own = static_cast<uint8_t*>(g->bases[rank]);
     int* xstatus = reinterpret_cast<int*>(own + P.ctrl + kCtrlStatus);
-    void* ws = own + P.ws[p];
+    void* ws = own + P.ws;
     cudaError_t err;
     timer_begin(st);  // stages as dsv41_moe_forward; permute includes publish + gather, combine the wait + sum
     // 1. publish this rank's tokens; the launch's last block stamps in_flag[rank] on every peer
@@ -640,7 +642,7 @@ int dsv41_ep_peer_read_status(const dsv41_ep_peer_group* g, const dsv41_moe_laye
                                           local_layer->intermediate, fat);
     uint8_t* own = static_cast<uint8_t*>(g->bases[g->rank]);
     int worst = 0;
-    const size_t words[3] = {P.ctrl + kCtrlStatus, P.ws[0] + P.L.status, P.ws[1] + P.L.status};
+    const size_t words[2] = {P.ctrl + kCtrlStatus, P.ws + P.L.status};
     for (size_t off : words) {
         int32_t v = 0;
         if ((rc = dsv41_read_status(own + off, stream, &v))) return rc;

@@ -3,7 +3,8 @@
 Each rank holds its shard E/world of a synthetic BASELINE-shape layer and routes its own 64 tokens over
 all global experts; the expert-parallel output (NCCL all-to-all dispatch/combine) must match the
 single-GPU layer (every rank also builds the full layer) within the parity bar; then the same for
-the peer-memory path (EPPeerMoE: token rows and expert outputs read from peers, no collective); last,
+the peer-memory path (EPPeerMoE: token rows read from peers, expert outputs stored into the token
+owners' memory, no collective), at decode and at prefill sizes; last,
 a rank that skips one step makes the other ranks' exchange waits run out (status 1, bounded at 50 ms)."""
 import datetime
 import os
@@ -23,6 +24,7 @@ from dsv41_flash_offload_b200 import exl3, synth  # noqa: E402
 from dsv41_flash_offload_b200.ep import EPMoE, EPPeerMoE, local_layer_fn  # noqa: E402
 
 E, H, I, K, T = 384, 4096, 2048, 8, 64
+TB = 1536   # tokens per rank of the prefill-sized peer steps (world * TB * K > 8192 gathered routes)
 
 
 def main():
@@ -69,6 +71,21 @@ def main():
         assert_close_layer(out.cpu().numpy(), ref.cpu().numpy(), f"peer rank {rank} case {case}")
     assert peer.read_status() == 0
     peer.close()
+    # prefill-sized steps: more gathered routes than the single-CTA permutation takes (separate gather
+    # launch + multi-CTA permutation) and busy experts on the tcgen05 GEMM, whose down epilogue stores the
+    # output rows into the token owners' receive slots
+    big = EPPeerMoE(shard, E, tokens_cap=TB, topk=K, limit=10.0)
+    for case in range(2):
+        seed = 800 + 10 * case + rank
+        x = torch.from_numpy(synth.hidden_np(seed, TB, H)).to(dev, torch.bfloat16)
+        ids_np, w_np = synth.routing_np(seed, TB, E, K, kind="zipf", zipf_s=1.1 if case == 0 else 1.5)
+        ids, w = torch.from_numpy(ids_np).to(dev), torch.from_numpy(w_np).to(dev)
+        out = big(x, ids, w)
+        ref = exl3.apply_exl3_fused_moe(x, ids, w, full, None, None, 10.0)
+        torch.cuda.synchronize()
+        assert_close_layer(out.cpu().numpy(), ref.cpu().numpy(), f"peer prefill rank {rank} case {case}")
+    assert big.read_status() == 0
+    big.close()
     expired = wait_expiry(shard, full, dev, rank, world)
     dist.barrier()
     print(f"rank {rank}/{world} ok: sent {ep.stats['sent_rows']} rows, received {ep.stats['recv_rows']}; "
