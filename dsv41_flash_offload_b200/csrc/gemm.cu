@@ -46,6 +46,9 @@ constexpr int kGemmThreads = (kWarpDec0 + kDecWarps) * 32;   // 384
 #define DSV41_GEMM_DEC_UNROLL 4
 #endif
 constexpr int kDecUnroll = DSV41_GEMM_DEC_UNROLL;   // tiles of the decode loop in flight per warp
+#ifndef DSV41_GEMM_PAIRED
+#define DSV41_GEMM_PAIRED 1   // decode a warp's tiles 2 (1 or 2), 4 or 8 at a time, states interleaved (K = 3)
+#endif
 #ifndef DSV41_GEMM_IMAD_PACKS
 #define DSV41_GEMM_IMAD_PACKS 4   // of the 4 half2 code packs per lane and tile, how many on IMAD
 #endif
@@ -564,12 +567,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
                 }
                 const uint32_t* trw = reinterpret_cast<const uint32_t*>(stage_t(st, dmat, dkt));
                 const uint32_t bt = smem_addr(stage_b(sb, dmat) + nt0 * 2 * kAtom) + soff;
+#if DSV41_GEMM_PAIRED && DSV41_CODES_WIN2
+                if constexpr (K == 3 && ntn % DSV41_GEMM_PAIRED == 0) {
+                    constexpr int NP = DSV41_GEMM_PAIRED == 1 ? 2 : DSV41_GEMM_PAIRED;   // tiles interleaved
+#pragma unroll
+                    for (int j = 0; j < ntn; j += NP) {
+                        const uint32_t* tw = trw + (nt0 + j) * TileFmt<K>::words;
+                        uint32_t b[NP][4];
+                        decode_tiles_codes3<NP, DSV41_GEMM_IMAD_PACKS>(tw, lw, k16, b);
+#pragma unroll
+                        for (int n = 0; n < NP; ++n) stmatrix_x4(bt + (j + n) * 2 * kAtom, b[n]);
+                    }
+                } else
+#endif
+                {
 #pragma unroll kDecUnroll
                 for (int j = 0; j < ntn; ++j) {
                     const uint32_t* tw = trw + (nt0 + j) * TileFmt<K>::words;
                     uint32_t b[4];
                     decode_tile_codes<K, DSV41_GEMM_IMAD_PACKS>(tw, lw, k16, b);   // affine codes: the epilogue applies KINV, KBIAS
                     stmatrix_x4(bt + j * 2 * kAtom, b);
+                }
                 }
                 fence_async_smem();
                 __syncwarp();

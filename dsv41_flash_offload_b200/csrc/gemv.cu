@@ -59,6 +59,10 @@ namespace dsv41 {
 #define DSV41_GEMV_IMAD_PACKS 3       // of the 4 half2 code packs per lane and tile, how many on IMAD (measured 2: 1.577, 3: 1.556, 4: 1.576 ms GEMV at T=64)
 #endif
 
+#ifndef DSV41_GEMV_PAIRED
+#define DSV41_GEMV_PAIRED 1           // decode a warp's two tiles with their states interleaved (K = 3)
+#endif
+
 #ifndef DSV41_GEMV_ROW_UNROLL
 #define DSV41_GEMV_ROW_UNROLL 16      // k-rows of a stage unrolled in the consumer loop
 #endif
@@ -147,6 +151,20 @@ __device__ __forceinline__ void gemv_stage(const uint32_t* trow, uint32_t xaddr,
         const uint32_t ones[4] = {0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u};
         mma_16816(rs[0], ones, bx[0], bx[1]);
         if (TWO) mma_16816(rs[1], ones, bx[2], bx[3]);
+#endif
+#if DSV41_GEMV_AFFINE && DSV41_GEMV_PAIRED && DSV41_CODES_WIN2
+        if constexpr (K == 3 && kTilesPerWarp == 2) {
+            uint32_t b[2][4];
+            decode_tiles_codes3<2, DSV41_GEMV_IMAD_PACKS>(trow + r * kRowWords, lw, k16, b);
+            const uint32_t a0[4] = {b[0][0], b[0][2], b[0][1], b[0][3]}, a1[4] = {b[1][0], b[1][2], b[1][1], b[1][3]};
+            mma_16816(acc[0][0], a0, bx[0], bx[1]);
+            mma_16816(acc[1][0], a1, bx[0], bx[1]);
+            if (TWO) {
+                mma_16816(acc[0][1], a0, bx[2], bx[3]);
+                mma_16816(acc[1][1], a1, bx[2], bx[3]);
+            }
+            continue;
+        }
 #endif
 #pragma unroll
         for (int t = 0; t < kTilesPerWarp; ++t) {
