@@ -101,6 +101,10 @@ __device__ __forceinline__ void had128_lanes(float (&v)[128 / L], int hl)
 #define DSV41_PREP_MIN_BLOCKS 4   // resident blocks per SM (measured on the 16k prefill: 4 lanes x 2 blocks 1.07 ms, 8 x 3 0.93, 8 x 4 0.87)
 #endif
 constexpr int kPrepLanes = DSV41_PREP_LANES;
+// CTA_ROW: one CTA per sorted row, its 8 warps splitting the row's 128-blocks (calls with few rows: decode
+// batches; measured at T=64 22.7 -> 11.6 us, T=1 18.7 -> 8.3 us); otherwise one warp per row (the prefill:
+// 0.89 ms at 16k tokens against 1.02 ms for the CTA form)
+template <bool CTA_ROW>
 __global__ void __launch_bounds__(256, DSV41_PREP_MIN_BLOCKS)
     prep_kernel(const __grid_constant__ XRows x, int x_dtype, const int* token_sorted, const int* expert_sorted,
                 const int* nrows, const __half* w13_suh, int H, __half* xt_g, __half* xt_u, float* rsum)
@@ -108,11 +112,17 @@ __global__ void __launch_bounds__(256, DSV41_PREP_MIN_BLOCKS)
     constexpr int L = kPrepLanes, V = 128 / L, BPW = 32 / L;   // lanes per block, values per lane, blocks per warp
     const int lane = threadIdx.x & 31, hl = lane % L, g = lane / L;
     const int nvalid = *nrows;
-    const int nb = H / 128, nit = (nb + BPW - 1) / BPW;
-    const int wstride = gridDim.x * (blockDim.x >> 5);
-    for (int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < nvalid; p += wstride) {
+    const int nb = H / 128;
+    // CTA_ROW: warp w transforms blocks BPW * (w + 8 j) + g of the CTA's row, and the row sums of the 8
+    // warps are added in warp order through shared memory
+    __shared__ float wsum[8][2];
+    const int warp = threadIdx.x >> 5;
+    const int nit = CTA_ROW ? (nb + 8 * BPW - 1) / (8 * BPW) : (nb + BPW - 1) / BPW;
+    const int p0 = CTA_ROW ? (int)blockIdx.x : (int)(blockIdx.x * (blockDim.x >> 5) + warp);
+    const int pstride = CTA_ROW ? (int)gridDim.x : (int)(gridDim.x * (blockDim.x >> 5));
+    for (int p = p0; p < nvalid; p += pstride) {
         const int e = expert_sorted[p];
-        if (e < 0) continue;
+        if (e < 0) continue;   // uniform over the CTA in the CTA_ROW form
         const int t = token_sorted[p];
         // token t's row: the caller's rows, or (expert parallel) row t % per of rank t / per
         const void* xb = x.base[0];
@@ -124,7 +134,7 @@ __global__ void __launch_bounds__(256, DSV41_PREP_MIN_BLOCKS)
         const __half* sg = w13_suh + (size_t)e * 2 * H;
         float sum[2] = {0.0f, 0.0f};
         for (int j = 0; j < nit; ++j) {
-            const int blk = BPW * j + g;
+            const int blk = CTA_ROW ? BPW * (warp + 8 * j) + g : BPW * j + g;
             const bool act = blk < nb;   // lanes past the last block transform a copy of block 0, unstored
             const int c = (act ? blk : 0) * 128 + hl * V;
             float xv[V];
@@ -165,7 +175,24 @@ __global__ void __launch_bounds__(256, DSV41_PREP_MIN_BLOCKS)
             for (int m = 0; m < 2; ++m)
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) sum[m] += __shfl_xor_sync(0xffffffffu, sum[m], o);
-            if (lane == 0) *reinterpret_cast<float2*>(rsum + 2 * (size_t)p) = make_float2(sum[0], sum[1]);
+            if (CTA_ROW) {
+                if (lane == 0) {
+                    wsum[warp][0] = sum[0];
+                    wsum[warp][1] = sum[1];
+                }
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    float a = 0.0f, b = 0.0f;
+                    for (int w = 0; w < 8; ++w) {
+                        a += wsum[w][0];
+                        b += wsum[w][1];
+                    }
+                    *reinterpret_cast<float2*>(rsum + 2 * (size_t)p) = make_float2(a, b);
+                }
+                __syncthreads();
+            } else if (lane == 0) {
+                *reinterpret_cast<float2*>(rsum + 2 * (size_t)p) = make_float2(sum[0], sum[1]);
+            }
         }
     }
 }
@@ -185,12 +212,19 @@ cudaError_t launch_prep_rows(const XRows& x, int x_dtype, const int* token_sorte
                              const int* nrows, int N, const __half* w13_suh, int H, __half* xt_g, __half* xt_u,
                              float* rsum, cudaStream_t st)
 {
-    long long blocks = ((long long)N + 7) / 8;   // one warp per sorted row
+    // rows of the call's bound: few rows (up to 32 per SM: decode batches, also expert-parallel ones whose
+    // bound counts every rank's routes) take one CTA each, more take one warp each
+    const bool cta_row = (long long)N <= (long long)num_sms() * 32;
+    long long blocks = cta_row ? (long long)N : ((long long)N + 7) / 8;
     const long long cap = (long long)num_sms() * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    prep_kernel<<<(int)blocks, 256, 0, st>>>(x, x_dtype, token_sorted, expert_sorted, nrows, w13_suh, H, xt_g,
-                                             xt_u, rsum);
+    if (cta_row)
+        prep_kernel<true><<<(int)blocks, 256, 0, st>>>(x, x_dtype, token_sorted, expert_sorted, nrows, w13_suh, H, xt_g,
+                                                       xt_u, rsum);
+    else
+        prep_kernel<false><<<(int)blocks, 256, 0, st>>>(x, x_dtype, token_sorted, expert_sorted, nrows, w13_suh, H,
+                                                        xt_g, xt_u, rsum);
     return cudaGetLastError();
 }
 
@@ -211,17 +245,30 @@ __global__ void __launch_bounds__(256) combine_kernel(const __half* y, const int
 #pragma unroll
             for (int q = 0; q < 8; ++q) acc[q] = 0.0f;
         }
-        for (int j = 0; j < topk; ++j) {
-            const int pos = route_pos[t * topk + j];
-            if (pos < 0) continue;
-            const float wt = w[t * topk + j];
-            const uint4 u = *reinterpret_cast<const uint4*>(y + (size_t)pos * H + c);
-            const uint32_t v[4] = {u.x, u.y, u.z, u.w};
+        // routes in groups of 8: every route position, weight and output row of the group is loaded before
+        // the first of them is added (three dependent memory round trips per group instead of two per route);
+        // the sum still runs over the routes in order
+        for (int j0 = 0; j0 < topk; j0 += 8) {
+            int pos[8];
+            float wt[8];
+            uint4 u[8];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const __half2 h = u32_as_half2(v[q]);
-                acc[2 * q] = __fmaf_rn(wt, __low2float(h), acc[2 * q]);
-                acc[2 * q + 1] = __fmaf_rn(wt, __high2float(h), acc[2 * q + 1]);
+            for (int jj = 0; jj < 8; ++jj) pos[jj] = j0 + jj < topk ? route_pos[t * topk + j0 + jj] : -1;
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+                wt[jj] = pos[jj] >= 0 ? w[t * topk + j0 + jj] : 0.0f;
+                u[jj] = pos[jj] >= 0 ? *reinterpret_cast<const uint4*>(y + (size_t)pos[jj] * H + c) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+                if (pos[jj] < 0) continue;
+                const uint32_t v[4] = {u[jj].x, u[jj].y, u[jj].z, u[jj].w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const __half2 h = u32_as_half2(v[q]);
+                    acc[2 * q] = __fmaf_rn(wt[jj], __low2float(h), acc[2 * q]);
+                    acc[2 * q + 1] = __fmaf_rn(wt[jj], __high2float(h), acc[2 * q + 1]);
+                }
             }
         }
         *reinterpret_cast<float4*>(o) = make_float4(acc[0], acc[1], acc[2], acc[3]);
