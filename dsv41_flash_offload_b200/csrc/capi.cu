@@ -313,11 +313,19 @@ static void timer_end(cudaStream_t st)
     g_timer.active = false;
 }
 
-// gate/up pass (GEMV groups, then GEMM for fat experts) and down pass over prepared rows
+// the decode-GEMV's ticket and ready counters within the workspace's counter block (after the split-K
+// arrival counters)
+static int* gemv_sched(int* counters, int groups_bound, int H, int I, int split)
+{
+    return counters + gemv_units_alloc(groups_bound, H, I, split) / split + 1;
+}
+
+// gate/up pass (GEMV groups, then GEMM for fat experts) and down pass over prepared rows; with
+// sched_cleared the caller has zeroed the decode-GEMV counters (and the split-K ones) already
 static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuffers& pb, __half* xt_g, __half* xt_u,
                                      __half* xt_d, __half* y, float* partials, int* counters, int* status, int split,
                                      int groups_bound, int rows_bound, float limit, int fat, uint8_t* gemm_scratch,
-                                     cudaStream_t st, const RowPush& push = RowPush{})
+                                     cudaStream_t st, const RowPush& push = RowPush{}, bool sched_cleared = false)
 {
     const int H = layer->hidden, I = layer->intermediate;
     // an expert takes the GEMM path with more than `fat` rows; no expert has more rows than the call's
@@ -326,8 +334,8 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
     cudaError_t err;
     // the split-K arrival counters, then the GEMV launches' ticket and ready counters
     const int n_split_counters = gemv_units_alloc(groups_bound, H, I, split) / split + 1;
-    int* sched = counters + n_split_counters;
-    if (split > 1) {
+    int* sched = gemv_sched(counters, groups_bound, H, I, split);
+    if (split > 1 && !sched_cleared) {
         const size_t n = (size_t)(n_split_counters + gemv_sched_ints(groups_bound)) * 4;
         if ((err = cudaMemsetAsync(counters, 0, n, st)) != cudaSuccess) return err;
     }
@@ -378,7 +386,8 @@ static cudaError_t run_expert_passes(const dsv41_moe_layer* layer, const PermBuf
     gd.N = H;
     if (split == 1) {
         // both decode-GEMV passes in one launch (stage "gemv_gateup"; "gemv_down" stays empty)
-        if ((err = launch_gemv_passes(gp, gd, 0, 1, sched, groups_bound, true, st)) != cudaSuccess) return err;
+        if ((err = launch_gemv_passes(gp, gd, 0, 1, sched, groups_bound, !sched_cleared, st)) != cudaSuccess)
+            return err;
         timer_mark(st, 3);
         if (gemm_on && (err = launch_gemm_gateup(ga, st)) != cudaSuccess) return err;
         timer_mark(st, 4);
@@ -450,6 +459,17 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
     cudaError_t err;
     const PermBuffers pb = perm_buffers(workspace, L);
     int* status = at<int>(workspace, L.status);
+    // the decode-GEMV's counters (split-K arrivals, tickets, ready counts) are cleared before the first
+    // kernel, so the chain of kernels below has no memset node between two kernels and every launch of it
+    // can be programmatic
+    int* counters = at<int>(workspace, L.counters);
+    {
+        int* from = L.split == 1 ? gemv_sched(counters, L.groups_bound, H, I, 1) : counters;
+        int* to = gemv_sched(counters, L.groups_bound, H, I, L.split) + gemv_sched_ints(L.groups_bound);
+        if ((err = cudaMemsetAsync(from, 0, (size_t)(to - from) * 4, st)) != cudaSuccess)
+            return cuda_fail(err, "clear the decode-GEMV counters");
+    }
+    const PdlScope pdl;
     timer_begin(st);
     if ((err = launch_permute(ids, weights, L.N, topk, E, o.expert_map, o.map_len, fat, pb, st)) !=
         cudaSuccess)
@@ -464,9 +484,9 @@ int dsv41_moe_forward(const dsv41_moe_layer* layer, const void* x, int32_t x_dty
                            gemm_sums(workspace, L, fat), st)) != cudaSuccess)
         return cuda_fail(err, "prep");
     timer_mark(st, 2);
-    if ((err = run_expert_passes(layer, pb, xt_g, xt_u, xt_d, y, at<float>(workspace, L.partials),
-                                 at<int>(workspace, L.counters), status, L.split, L.groups_bound, L.rows, o.limit,
-                                 fat, at<uint8_t>(workspace, L.gemm), st)) != cudaSuccess)
+    if ((err = run_expert_passes(layer, pb, xt_g, xt_u, xt_d, y, at<float>(workspace, L.partials), counters, status,
+                                 L.split, L.groups_bound, L.rows, o.limit, fat, at<uint8_t>(workspace, L.gemm), st,
+                                 RowPush{}, /*sched_cleared=*/true)) != cudaSuccess)
         return cuda_fail(err, "expert passes");
     if ((err = launch_combine(y, pb.route_pos, weights, T, topk, H, 0, out, st)) != cudaSuccess)
         return cuda_fail(err, "combine");

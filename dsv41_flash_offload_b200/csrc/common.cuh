@@ -421,6 +421,16 @@ __device__ __forceinline__ uint64_t globaltimer_ns()
 }
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s, as the reference's combine wait
+
+// programmatic dependent launch (see launch_k in internal.h): wait for the preceding grid on the stream
+// (a no-op for a kernel launched without the attribute), then let the next grid be scheduled
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void griddep_enter()
+{
+    griddep_wait();
+    griddep_launch_dependents();
+}
 #ifndef DSV41_WAIT_HINT_NS
 #define DSV41_WAIT_HINT_NS 20000   // suspend hint of one try_wait (0: poll without suspending)
 #endif

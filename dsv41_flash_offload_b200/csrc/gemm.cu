@@ -328,6 +328,7 @@ __device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128])
 template <int MODE, int K>
 __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid_constant__ GemmParams p)
 {
+    griddep_enter();
     using Cfg = GemmCfg<MODE, K>;
     constexpr int kTrRow = tr_row<K>();
     constexpr int AS = Cfg::a_stages, BS = Cfg::b_stages, TS = Cfg::t_stages;
@@ -679,6 +680,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) exl3_gemm_kernel(const __grid
 __global__ void gemm_plan_kernel(const int* fat_experts, const int* n_fat, const int* counts, const int* offsets,
                                  int rp0, int rp1, int4* passes0, int* n0, int4* passes1, int* n1)
 {
+    griddep_enter();
     if (threadIdx.x != 0) return;
     const int nf = *n_fat;
     int a = 0, b = 0;
@@ -756,9 +758,9 @@ static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
     cudaError_t err;
     if (MODE == 0) {
         const int rp0 = GemmCfg<0, K>::rows_per_pass, rp1 = GemmCfg<1, K>::rows_per_pass;
-        gemm_plan_kernel<<<1, 32, 0, st>>>(a.fat_experts, a.n_fat, a.counts, a.offsets, rp0, rp1, passes0, counters, passes1,
-                                           counters + 1);
-        if ((err = cudaGetLastError()) != cudaSuccess) return err;
+        if ((err = launch_k(gemm_plan_kernel, 1, 32, 0, st, a.fat_experts, a.n_fat, a.counts, a.offsets, rp0, rp1,
+                            passes0, counters, passes1, counters + 1)) != cudaSuccess)
+            return err;
     }
     GemmParams p{};
     if (MODE == 0) {
@@ -802,8 +804,7 @@ static cudaError_t launch_mode(const GemmArgs& a, cudaStream_t st)
     int grid = num_sms();
     if (units_bound < grid) grid = units_bound;
     if (grid < 1) grid = 1;
-    exl3_gemm_kernel<MODE, K><<<grid, kGemmThreads, smem, st>>>(p);
-    return cudaGetLastError();
+    return launch_k(exl3_gemm_kernel<MODE, K>, grid, kGemmThreads, smem, st, p);
 }
 
 static int args_bits(const GemmArgs& a) { return a.layer->bits ? a.layer->bits : 3; }

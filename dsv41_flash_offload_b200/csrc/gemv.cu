@@ -454,6 +454,7 @@ template <int K, int KS>
 __global__ void __launch_bounds__(gemv_threads<KS>(), KS == 1 ? DSV41_GEMV_MIN_BLOCKS : 1)
     exl3_gemv_kernel(const __grid_constant__ GemvWork w)
 {
+    griddep_enter();
     constexpr int kConsumerWarps = consumer_warps<KS>();
     constexpr int kStages = gemv_stages<KS>();
     using Smem = GemvSmem<K, kStages>;
@@ -573,8 +574,7 @@ static cudaError_t launch_work_k(const GemvWork& w, int units_bound, cudaStream_
     int grid = (KS == 1 ? DSV41_GEMV_MIN_BLOCKS : 1) * num_sms();
     if (units_bound < grid) grid = units_bound;
     if (grid < 1) grid = 1;
-    exl3_gemv_kernel<K, KS><<<grid, gemv_threads<KS>(), smem, st>>>(w);
-    return cudaGetLastError();
+    return launch_k(exl3_gemv_kernel<K, KS>, grid, gemv_threads<KS>(), smem, st, w);
 }
 
 // calls whose passes each fit in one CTA per SM run the 16-warp form (twice the warps per unit)

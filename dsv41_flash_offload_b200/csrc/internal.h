@@ -164,6 +164,40 @@ cudaError_t launch_wait_selftest(int* status, uint64_t limit_ns, cudaStream_t st
 
 int num_sms();
 
+// Programmatic dependent launch for the kernels of one single-GPU layer forward (dsv41_moe_forward):
+// while a PdlScope is alive on this thread, launch_k gives each launch the programmatic stream
+// serialization attribute, so a kernel can be scheduled while the one before it on the stream finishes
+// (its launch and prologue overlap the predecessor's tail). Every kernel launched this way begins with
+// griddep_wait() (common.cuh), which returns once the preceding grid has completed and its memory is
+// visible, and only then touches data another kernel wrote; launched without the attribute the wait
+// returns at once.
+#ifndef DSV41_PDL
+#define DSV41_PDL 1   // 0: plain launches everywhere
+#endif
+inline thread_local int g_pdl_scopes = 0;
+struct PdlScope {
+    PdlScope() { ++g_pdl_scopes; }
+    ~PdlScope() { --g_pdl_scopes; }
+};
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args... args)
+{
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (DSV41_PDL && g_pdl_scopes > 0) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // record a message for dsv41_last_error() and return `code`
 int set_error(int code, const char* fmt, ...);
 

@@ -169,6 +169,7 @@ __device__ void walk_segment(const PermArgs& a, int b, int e, int* row, const in
 // Single CTA (N <= kPermSmallMax): 32 warp segments, all phases in shared memory.
 __global__ void __launch_bounds__(1024) permute_small_kernel(const PermArgs a)
 {
+    griddep_enter();
     extern __shared__ int sm[];
     const int E1 = a.E + 1;
     int* seg = sm;                    // [32][E1]
@@ -209,6 +210,7 @@ constexpr int kPermWarps = 8;
 
 __global__ void __launch_bounds__(kPermWarps * 32) permute_hist_kernel(const PermArgs a)
 {
+    griddep_enter();
     extern __shared__ int sm[];
     const int E1 = a.E + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -226,6 +228,7 @@ __global__ void __launch_bounds__(kPermWarps * 32) permute_hist_kernel(const Per
 
 __global__ void __launch_bounds__(1024) permute_scan_kernel(const PermArgs a)
 {
+    griddep_enter();
     extern __shared__ int sm[];
     const int E1 = a.E + 1;
     int* tot = sm;
@@ -248,6 +251,7 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(const PermArgs a)
 
 __global__ void __launch_bounds__(kPermWarps * 32) permute_scatter_kernel(const PermArgs a)
 {
+    griddep_enter();
     extern __shared__ int sm[];
     const int E1 = a.E + 1;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -364,8 +368,7 @@ cudaError_t launch_permute(const int64_t* ids, const float* weights, int N, int 
     if (perm_uses_small(N, E)) {
         const size_t smem = (32 * E1 + 2 * E1 + 33) * sizeof(int);
         if ((err = set_smem((const void*)permute_small_kernel, smem)) != cudaSuccess) return err;
-        permute_small_kernel<<<1, 1024, smem, st>>>(a);
-        return cudaGetLastError();
+        return launch_k(permute_small_kernel, 1, 1024, smem, st, a);
     }
     const int nseg = (N + kPermSegment - 1) / kPermSegment;
     const int blocks = (nseg + kPermWarps - 1) / kPermWarps;
@@ -375,10 +378,9 @@ cudaError_t launch_permute(const int64_t* ids, const float* weights, int N, int 
     if ((err = set_smem((const void*)permute_hist_kernel, smem_h)) != cudaSuccess) return err;
     if ((err = set_smem((const void*)permute_scan_kernel, smem_s)) != cudaSuccess) return err;
     if ((err = set_smem((const void*)permute_scatter_kernel, smem_x)) != cudaSuccess) return err;
-    permute_hist_kernel<<<blocks, kPermWarps * 32, smem_h, st>>>(a);
-    permute_scan_kernel<<<1, 1024, smem_s, st>>>(a);
-    permute_scatter_kernel<<<blocks, kPermWarps * 32, smem_x, st>>>(a);
-    return cudaGetLastError();
+    if ((err = launch_k(permute_hist_kernel, blocks, kPermWarps * 32, smem_h, st, a)) != cudaSuccess) return err;
+    if ((err = launch_k(permute_scan_kernel, 1, 1024, smem_s, st, a)) != cudaSuccess) return err;
+    return launch_k(permute_scatter_kernel, blocks, kPermWarps * 32, smem_x, st, a);
 }
 
 cudaError_t launch_permute_gathered(const EpGather& g, int topk, int E, int fat_threshold, const PermBuffers& pb,

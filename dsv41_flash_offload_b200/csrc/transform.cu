@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(256, DSV41_PREP_MIN_BLOCKS)
     prep_kernel(const __grid_constant__ XRows x, int x_dtype, const int* token_sorted, const int* expert_sorted,
                 const int* nrows, const __half* w13_suh, int H, __half* xt_g, __half* xt_u, float* rsum)
 {
+    griddep_enter();
     constexpr int L = kPrepLanes, V = 128 / L, BPW = 32 / L;   // lanes per block, values per lane, blocks per warp
     const int lane = threadIdx.x & 31, hl = lane % L, g = lane / L;
     const int nvalid = *nrows;
@@ -219,19 +220,15 @@ cudaError_t launch_prep_rows(const XRows& x, int x_dtype, const int* token_sorte
     const long long cap = (long long)num_sms() * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    if (cta_row)
-        prep_kernel<true><<<(int)blocks, 256, 0, st>>>(x, x_dtype, token_sorted, expert_sorted, nrows, w13_suh, H, xt_g,
-                                                       xt_u, rsum);
-    else
-        prep_kernel<false><<<(int)blocks, 256, 0, st>>>(x, x_dtype, token_sorted, expert_sorted, nrows, w13_suh, H,
-                                                        xt_g, xt_u, rsum);
-    return cudaGetLastError();
+    return launch_k(cta_row ? prep_kernel<true> : prep_kernel<false>, (int)blocks, 256, 0, st, x, x_dtype, token_sorted,
+                    expert_sorted, nrows, w13_suh, H, xt_g, xt_u, rsum);
 }
 
 // thread = (token t, 8 consecutive columns)
 __global__ void __launch_bounds__(256) combine_kernel(const __half* y, const int* route_pos, const float* w, int T,
                                                       int topk, int H, int accumulate, float* out)
 {
+    griddep_enter();
     const int chunks = H / 8;
     const long long n = (long long)T * chunks;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
@@ -284,8 +281,7 @@ cudaError_t launch_combine(const __half* y, const int* route_pos, const float* w
     const long long cap = (long long)num_sms() * 16;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    combine_kernel<<<(int)blocks, 256, 0, st>>>(y, route_pos, w, T, topk, H, accumulate, out);
-    return cudaGetLastError();
+    return launch_k(combine_kernel, (int)blocks, 256, 0, st, y, route_pos, w, T, topk, H, accumulate, out);
 }
 
 // Busy-expert rows accumulated into out with fp32 atomics (the reference fat path accumulates
