@@ -588,6 +588,16 @@ int dsv41_ep_peer_forward(const dsv41_moe_layer* local_layer, const dsv41_ep_pee
     int* xstatus = reinterpret_cast<int*>(own + P.ctrl + kCtrlStatus);
     void* ws = own + P.ws;
     cudaError_t err;
+    // the decode-GEMV's counters cleared before the first kernel (no memset node inside the kernel chain,
+    // whose launches are programmatic as in dsv41_moe_forward)
+    {
+        int* counters = at<int>(ws, L.counters);
+        int* from = L.split == 1 ? gemv_sched(counters, L.groups_bound, H, I, 1) : counters;
+        int* to = gemv_sched(counters, L.groups_bound, H, I, L.split) + gemv_sched_ints(L.groups_bound);
+        if ((err = cudaMemsetAsync(from, 0, (size_t)(to - from) * 4, st)) != cudaSuccess)
+            return cuda_fail(err, "clear the decode-GEMV counters");
+    }
+    const PdlScope pdl;
     timer_begin(st);  // stages as dsv41_moe_forward; permute includes publish + gather, combine the wait + sum
     // 1. publish this rank's tokens; the launch's last block stamps in_flag[rank] on every peer
     if ((err = launch_ep_publish(x, x_dtype, ids, weights, T, tcap, k, E, H, reinterpret_cast<__half*>(own + P.x[p]),
@@ -632,7 +642,7 @@ int dsv41_ep_peer_forward(const dsv41_moe_layer* local_layer, const dsv41_ep_pee
     if ((err = run_expert_passes(local_layer, pb, at<__half>(ws, L.xt_g), at<__half>(ws, L.xt_u),
                                  at<__half>(ws, L.xt_d), at<__half>(ws, L.y), at<float>(ws, L.partials),
                                  at<int>(ws, L.counters), at<int>(ws, L.status), L.split, L.groups_bound, L.rows, limit,
-                                 fat, at<uint8_t>(ws, L.gemm), st, push)) != cudaSuccess)
+                                 fat, at<uint8_t>(ws, L.gemm), st, push, /*sched_cleared=*/true)) != cudaSuccess)
         return cuda_fail(err, "expert passes");
     // 5. outputs delivered: drop flag + out stamp on every peer; 6. sum this rank's routes from its slots
     if ((err = launch_ep_signal(peers, world, rank, P.ctrl + kCtrlOutFlags, stamp, pb.nrows, P.ctrl + kCtrlOutDrop,

@@ -34,6 +34,7 @@ __global__ void __launch_bounds__(256) ep_publish_kernel(const void* x, int x_dt
                                                          __half* X, int* IDS, float* W, PeerTable peers, int world,
                                                          int rank, size_t flag_off, uint32_t stamp, int* done)
 {
+    griddep_enter();
     const long long stride = (long long)gridDim.x * blockDim.x;
     const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const long long nx = (long long)T * H / 4;
@@ -76,6 +77,7 @@ __global__ void __launch_bounds__(256) ep_publish_kernel(const void* x, int x_dt
 __global__ void ep_signal_kernel(PeerTable peers, int world, int rank, size_t flag_off, uint32_t stamp,
                                  const int* nrows, size_t drop_off)
 {
+    griddep_enter();
     const int d = threadIdx.x;
     if (d >= world) return;
     uint8_t* b = static_cast<uint8_t*>(peers.base[d]);
@@ -86,6 +88,7 @@ __global__ void ep_signal_kernel(PeerTable peers, int world, int rank, size_t fl
 
 __global__ void __launch_bounds__(256) ep_gather_kernel(const EpGather g)
 {
+    griddep_enter();
     const bool ok = block_wait_stamps(g.in_flags, g.world, g.stamp, g.status, g.limit_ns);
     ep_gather_routes(g, ok, (long long)blockIdx.x * blockDim.x + threadIdx.x, (long long)gridDim.x * blockDim.x);
 }
@@ -101,6 +104,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const uint32_t* flags, 
                                                          int T, int k, int H, const __half* recv, float* out,
                                                          int* status, uint64_t limit_ns)
 {
+    griddep_enter();
     __shared__ float wts[kCombineRoutes];
     __shared__ int live[kCombineRoutes];
     const bool ok = block_wait_stamps(flags, world, stamp, status, limit_ns);
@@ -173,22 +177,19 @@ cudaError_t launch_ep_publish(const void* x, int x_dtype, const int64_t* ids, co
                               size_t flag_off, uint32_t stamp, int* done, cudaStream_t st)
 {
     const long long work = (long long)T * H / 4 > (long long)tcap * k ? (long long)T * H / 4 : (long long)tcap * k;
-    ep_publish_kernel<<<grid_for(work, 256, 8), 256, 0, st>>>(x, x_dtype, ids, w, T, tcap, k, E, H, X, IDS, W, peers,
-                                                              world, rank, flag_off, stamp, done);
-    return cudaGetLastError();
+    return launch_k(ep_publish_kernel, grid_for(work, 256, 8), 256, 0, st, x, x_dtype, ids, w, T, tcap, k, E, H, X, IDS,
+                    W, peers, world, rank, flag_off, stamp, done);
 }
 
 cudaError_t launch_ep_signal(const PeerTable& peers, int world, int rank, size_t flag_off, uint32_t stamp,
                              const int* nrows, size_t drop_off, cudaStream_t st)
 {
-    ep_signal_kernel<<<1, 32, 0, st>>>(peers, world, rank, flag_off, stamp, nrows, drop_off);
-    return cudaGetLastError();
+    return launch_k(ep_signal_kernel, 1, 32, 0, st, peers, world, rank, flag_off, stamp, nrows, drop_off);
 }
 
 cudaError_t launch_ep_gather(const EpGather& g, cudaStream_t st)
 {
-    ep_gather_kernel<<<grid_for((long long)g.world * g.per, 4 * 256, 4), 256, 0, st>>>(g);
-    return cudaGetLastError();
+    return launch_k(ep_gather_kernel, grid_for((long long)g.world * g.per, 4 * 256, 4), 256, 0, st, g);
 }
 
 cudaError_t launch_ep_combine(const uint32_t* out_flags, const uint32_t* drops, int world, int e_loc, uint32_t stamp,
@@ -196,9 +197,8 @@ cudaError_t launch_ep_combine(const uint32_t* out_flags, const uint32_t* drops, 
                               int* status, uint64_t limit_ns, cudaStream_t st)
 {
     if (H > 8 * 256 * 4) return cudaErrorInvalidValue;   // the combine's 4 chunks of 8 columns per thread
-    ep_combine_kernel<<<grid_for(T, 1, 8), 256, 0, st>>>(out_flags, drops, world, e_loc, stamp, ids, w, T, k, H, recv,
-                                                         out, status, limit_ns);
-    return cudaGetLastError();
+    return launch_k(ep_combine_kernel, grid_for(T, 1, 8), 256, 0, st, out_flags, drops, world, e_loc, stamp, ids, w, T,
+                    k, H, recv, out, status, limit_ns);
 }
 
 }  // namespace dsv41

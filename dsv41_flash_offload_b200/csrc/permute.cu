@@ -395,8 +395,7 @@ cudaError_t launch_permute_gathered(const EpGather& g, int topk, int E, int fat_
         const size_t smem = (32 * E1 + 2 * E1 + 33) * sizeof(int);
         cudaError_t err;
         if ((err = set_smem((const void*)permute_small_kernel, smem)) != cudaSuccess) return err;
-        permute_small_kernel<<<1, 1024, smem, st>>>(a);
-        return cudaGetLastError();
+        return launch_k(permute_small_kernel, 1, 1024, smem, st, a);
     }
     const cudaError_t err = launch_ep_gather(g, st);
     if (err != cudaSuccess) return err;
